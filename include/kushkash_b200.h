@@ -1,0 +1,116 @@
+/*
+ * kushkash_b200.h -- C ABI of libkush_sm100.so, the sm_100a (B200) kernels of kushkash's two hot paths:
+ * quantize-on-write into int4/int8 page records, and fused dequant paged decode attention.
+ *
+ * Each entry point replaces one GPU kernel of the reference (kushkash/kush/gpu.mojo), launched by the reference's
+ * ctypes loader (kushkash/_cuda.py:92-103, Kernel.__call__) from kushkash/_ops.py.  Arguments keep the reference
+ * kernel's order and meaning; what the reference fixes at compile time (head_dim, bits, q-heads-per-kv-head,
+ * dtype: kushkash/_build.py:269-306 GpuConfig) and its launch grid become leading / trailing plain arguments, plus
+ * the page size (16 or 32 tokens; kushkash fixes 32, kushkash/kush/quant.mojo:16).  Every pointer is a device
+ * address; strides are in elements unless named *_stride in bytes (block_stride, head_stride).  The kernels run
+ * on `stream` (a cudaStream_t; NULL = legacy default stream), allocate nothing and never synchronise the host.
+ *
+ * Return value: KUSH_OK, or a negative status; kush_sm100_last_error() then describes the failure.
+ */
+#ifndef KUSHKASH_B200_H
+#define KUSHKASH_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KUSH_OK 0
+#define KUSH_ERR_UNSUPPORTED (-1) /* head_dim / bits / page / dtype / group combination not built */
+#define KUSH_ERR_ARG (-2)         /* invalid argument: null pointer, misaligned address or stride, bad size */
+#define KUSH_ERR_CUDA (-3)        /* the launch failed: a CUDA error */
+
+/* element type of q, out, k/v rows and tail_k (the reference's IN: kushkash/_build.py:28) */
+#define KUSH_F16 0
+#define KUSH_BF16 1
+#define KUSH_F32 2
+
+/* Message of the last failed call made on this host thread ("" if none). */
+const char *kush_sm100_last_error(void);
+
+/* Library version string. */
+const char *kush_sm100_version(void);
+
+/* Bytes of one (page, kv head) record: 2*P*DC + 4*D + 4*P, DC = D (int8) or D/2 (int4)
+ * (kushkash/kush/quant.mojo:60-62, kushkash/_ops.py:29-31 record_bytes). 0 if unsupported. */
+int64_t kush_sm100_record_bytes(int32_t head_dim, int32_t bits, int32_t page);
+
+/* Decode append: one new token per sequence.  Replaces kush_append (kushkash/kush/gpu.mojo:207-238) as launched
+ * by Ops.append (kushkash/_ops.py:66-80).  Row s of k_new / v_new (row strides k_stride / v_stride, head h at
+ * +h*head_dim) goes to position seq_lens[s] + pos_offset (HF: 0 with advance = 1; vLLM: -1, seq_lens already
+ * counting the token); negative positions are skipped.  K goes to the exact tail tail_k[tail_idx[s]][h][slot],
+ * V is quantized into row `slot` of the page's record; the page's last slot quantizes its K from the tail.
+ * advance != 0 stores pos + 1 into seq_lens[s].  The token's page must be mapped in block_table
+ * ([n_seqs] rows, row stride max_pages). */
+int kush_sm100_append(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void *k_new,
+                      const void *v_new, int64_t k_stride, int64_t v_stride, int32_t *seq_lens, int32_t pos_offset,
+                      int32_t advance, const int32_t *tail_idx, void *cache, int64_t block_stride, int64_t head_stride,
+                      void *tail_k, const int32_t *block_table, int64_t max_pages, int32_t hkv, int32_t n_seqs,
+                      void *stream);
+
+/* Ragged multi-token write.  Replaces kush_write (kushkash/kush/gpu.mojo:241-276) as launched by Ops.write
+ * (kushkash/_ops.py:82-101).  Sequence s owns rows [query_start_loc[s], query_start_loc[s+1]) at positions
+ * ending at seq_lens[s]; job j covers logical page job_page[j] of sequence job_seq[j].  mode 0: write the page's
+ * new V rows and, for a page now complete, quantize its K (older rows from the tail, newer from the new rows);
+ * mode 1: copy a still-partial page's new K rows into the tail.  The reference launches mode 0 for every job,
+ * then mode 1.  mode 2 does both in ONE launch (the tail stash of a sequence runs in the CTA that reads the old
+ * tail, after it has read it), with the same result as mode 0 then mode 1. */
+int kush_sm100_write(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void *k_new,
+                     const void *v_new, int64_t k_stride, int64_t v_stride, const int32_t *query_start_loc,
+                     const int32_t *seq_lens, const int32_t *tail_idx, const int32_t *job_seq,
+                     const int32_t *job_page, int32_t mode, void *cache, int64_t block_stride, int64_t head_stride,
+                     void *tail_k, const int32_t *block_table, int64_t max_pages, int32_t hkv, int32_t n_jobs,
+                     void *stream);
+
+/* Fused dequant paged decode attention.  Replaces kush_decode_tc / kush_decode (kushkash/kush/gpu.mojo:566-807,
+ * 840-1040) as launched by Ops.decode (kushkash/_ops.py:191-211): out[s] ([hkv*group, head_dim], q head =
+ * kv_head*group + g) = attention of q[s] over the seq_lens[s] cached tokens of sequence s, softmax scale `scale`.
+ * Full pages come from the records, the last n % page tokens take K from the exact tail and V from their record.
+ * n_splits > 1 (split-KV / flash-decoding): split z of (s, h) owns a contiguous page range and writes its
+ * partial (M, L) to part_ml [n_seqs][hkv][n_splits][group][2] and unnormalised O to part_o
+ * [n_seqs][hkv][n_splits][group][head_dim] (fp32); kush_sm100_combine then writes out.  q, out contiguous. */
+int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group, const void *q,
+                      void *out, const void *cache, int64_t block_stride, int64_t head_stride, const void *tail_k,
+                      const int32_t *tail_idx, const int32_t *block_table, const int32_t *seq_lens, int64_t max_pages,
+                      int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o, int32_t n_seqs,
+                      void *stream);
+
+/* Split-KV merge.  Replaces kush_combine (kushkash/kush/gpu.mojo:469-491) as launched by Ops.decode
+ * (kushkash/_ops.py:212-213): out = sum_z exp(M_z - M) O_z / sum_z exp(M_z - M) L_z per (s, h, g). */
+int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void *out, const float *part_ml,
+                       const float *part_o, int32_t n_splits, int32_t hkv, int32_t n_seqs, void *stream);
+
+/* Which decode kernel a configuration takes: 1 = tensor-core kernel (mma), 0 = CUDA-core kernel,
+ * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
+int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);
+
+/* Canonical Walsh-Hadamard rotation of `rows` rows of head_dim values: y[r] = fwht(x[r]) (row strides in
+ * elements; y may alias x).  Replaces kush_fwht (kushkash/kush/gpu.mojo:95-112) as launched by Ops.fwht
+ * (kushkash/_ops.py:104-127): fp32 butterflies over strides 1, 2, ..., D/2 in that order, then one multiply by
+ * fp32 1/sqrt(D) (kushkash/kush/quant.mojo:90-122), bit-identical to the CPU. */
+int kush_sm100_fwht(int32_t head_dim, int32_t dtype, const void *x, void *y, int64_t x_stride, int64_t y_stride,
+                    int64_t rows, void *stream);
+
+/* Packed-prefill unpack.  Replaces kush_unpack (kushkash/kush/gpu.mojo:303-375) as launched by Ops.unpack
+ * (kushkash/_ops.py:129-179): full history pages (block page_blk[i] -> rows page_dst[i] + t), partial pages
+ * (block tail_blk[i], tail_info[3i..3i+2] = (first row, tokens, tail slot): K from tail_k, V from the record)
+ * and new rows (row j of k_new / v_new -> row new_dst[j]) into kp / vp ([rows][hkv][head_dim]).  History is
+ * dequantized as fma(code, scale, bias) in fp32, optionally rotated back (rot != 0), rounded once to dtype. */
+int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void *cache,
+                      int64_t block_stride, int64_t head_stride, int32_t hkv, const int32_t *page_blk,
+                      const int32_t *page_dst, int32_t n_pages, const int32_t *tail_blk, const int32_t *tail_info,
+                      int32_t n_tail, const void *tail_k, const void *k_new, const void *v_new, int64_t k_stride,
+                      int64_t v_stride, const int32_t *new_dst, int32_t n_new, void *kp, void *vp, int32_t rot,
+                      void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KUSHKASH_B200_H */

@@ -1,0 +1,160 @@
+"""ctypes shim over libkush_sm100.so: the B200 replacement of the reference's Mojo/PTX loader
+(kushkash/_cuda.py:14-117).
+
+Same contract: `kernels(device, cfg)` returns {name: callable(grid, block, *args)} for append, write, decode,
+combine, fwht and unpack, called with the reference's argument lists (kushkash/_ops.py:73-75, 93-96, 120, 177,
+209-213: raw data_ptr() ints, int32 scalars, one float softmax scale) and launched on torch's current stream of
+the device.  The callables translate the launch grid into the C ABI's sizes (include/kushkash_b200.h); the block
+size the reference passes is ignored, every kernel picks its own.
+
+There is no fallback: if the library is missing or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from functools import lru_cache
+from pathlib import Path
+
+import torch
+
+from ._build import GpuConfig
+
+LIB_PATH = Path(__file__).resolve().parent / "libkush_sm100.so"
+
+KUSH_OK, KUSH_ERR_UNSUPPORTED, KUSH_ERR_ARG, KUSH_ERR_CUDA = 0, -1, -2, -3
+
+_i32, _i64, _f32, _p = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+# argument types of every entry point declared in include/kushkash_b200.h
+SIGNATURES = {
+    "kush_sm100_append": [_i32, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _i32, _i32, _p, _p, _i64, _i64, _p, _p,
+                          _i64, _i32, _i32, _p],
+    "kush_sm100_write": [_i32, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _i64, _i64, _p, _p,
+                         _i64, _i32, _i32, _p],
+    "kush_sm100_decode": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32, _i32,
+                          _p, _p, _i32, _p],
+    "kush_sm100_combine": [_i32, _i32, _i32, _p, _p, _p, _i32, _i32, _i32, _p],
+    "kush_sm100_decode_tensor_cores": [_i32, _i32, _i32, _i32, _i32],
+    "kush_sm100_fwht": [_i32, _i32, _p, _p, _i64, _i64, _i64, _p],
+    "kush_sm100_unpack": [_i32, _i32, _i32, _i32, _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _i64,
+                          _i64, _p, _i32, _p, _p, _i32, _p],
+    "kush_sm100_record_bytes": [_i32, _i32, _i32],
+    "kush_sm100_last_error": [],
+    "kush_sm100_version": [],
+}
+
+
+@lru_cache(None)
+def lib() -> ctypes.CDLL:
+    """Load the kernel library (built in-tree by kushkash_b200/build.py); raises if it is missing."""
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m kushkash_b200.build` "
+                           "(kushkash_b200 has no CPU or PyTorch fallback)")
+    dll = ctypes.CDLL(str(LIB_PATH))
+    for name, args in SIGNATURES.items():
+        fn = getattr(dll, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int32
+    dll.kush_sm100_record_bytes.restype = ctypes.c_int64
+    dll.kush_sm100_last_error.restype = ctypes.c_char_p
+    dll.kush_sm100_version.restype = ctypes.c_char_p
+    return dll
+
+
+def last_error() -> str:
+    return (lib().kush_sm100_last_error() or b"").decode()
+
+
+def check(rc: int, what: str) -> None:
+    """Raise on a failed call: ValueError for an unsupported configuration or a bad argument (the reference raises
+    ValueError / BuildError there), RuntimeError for a CUDA error (as kushkash/_cuda.py:39-43 does)."""
+    if rc == KUSH_OK:
+        return
+    msg = last_error() or f"status {rc}"
+    if rc in (KUSH_ERR_UNSUPPORTED, KUSH_ERR_ARG):
+        raise ValueError(f"launch {what}: {msg}")
+    raise RuntimeError(f"launch {what}: {msg}")
+
+
+def raw_stream(device: int) -> int:
+    """torch's current stream of `device` (the reference launches there too, kushkash/_cuda.py:55-57)."""
+    return torch._C._cuda_getCurrentRawStream(device)
+
+
+def decode_tensor_cores(cfg: GpuConfig) -> bool:
+    rc = lib().kush_sm100_decode_tensor_cores(cfg.head_dim, cfg.bits, cfg.page, cfg.dtype_code, cfg.group)
+    if rc < 0:
+        raise ValueError(f"decode: unsupported configuration {cfg}")
+    return rc == 1
+
+
+class Kernel:
+    """One operation bound to (device, config): __call__(grid, block, *args) with the reference's argument list."""
+
+    def __init__(self, device: int, cfg: GpuConfig, name: str):
+        self.device, self.cfg, self.name = device, cfg, name
+        self.fn = getattr(lib(), "kush_sm100_" + name)
+        self._call = getattr(self, "_" + name)
+
+    def __call__(self, grid: tuple[int, int, int], block: int, *args) -> None:
+        with torch.cuda.device(self.device):
+            rc = self._call(grid, *args)
+        check(rc, f"kush_sm100_{self.name}")
+
+    # gpu.mojo:207-211 argument order
+    def _append(self, grid, k, v, ks, vs, seq_lens, pos_offset, advance, tail_idx, cache, bs, hs, tail_k, bt, max_pages,
+                hkv):
+        c = self.cfg
+        return self.fn(c.head_dim, c.bits, c.page, c.dtype_code, k, v, ks, vs, seq_lens, pos_offset, advance, tail_idx,
+                       cache, bs, hs, tail_k, bt, max_pages, hkv, grid[0], raw_stream(self.device))
+
+    # gpu.mojo:241-245 argument order
+    def _write(self, grid, k, v, ks, vs, qsl, seq_lens, tail_idx, job_seq, job_page, mode, cache, bs, hs, tail_k, bt,
+               max_pages, hkv):
+        c = self.cfg
+        return self.fn(c.head_dim, c.bits, c.page, c.dtype_code, k, v, ks, vs, qsl, seq_lens, tail_idx, job_seq,
+                       job_page, mode, cache, bs, hs, tail_k, bt, max_pages, hkv, grid[0], raw_stream(self.device))
+
+    # gpu.mojo:566-571 argument order
+    def _decode(self, grid, q, out, cache, bs, hs, tail_k, tail_idx, bt, seq_lens, max_pages, hkv, scale, n_splits,
+                part_ml, part_o):
+        c = self.cfg
+        return self.fn(c.head_dim, c.bits, c.page, c.dtype_code, c.group, q, out, cache, bs, hs, tail_k, tail_idx, bt,
+                       seq_lens, max_pages, hkv, scale, n_splits, part_ml or None, part_o or None, grid[0],
+                       raw_stream(self.device))
+
+    # gpu.mojo:469-470 argument order
+    def _combine(self, grid, out, part_ml, part_o, n_splits, hkv):
+        c = self.cfg
+        return self.fn(c.head_dim, c.dtype_code, c.group, out, part_ml, part_o, n_splits, hkv, grid[0],
+                       raw_stream(self.device))
+
+    # gpu.mojo:95-98 argument order
+    def _fwht(self, grid, x, y, x_stride, y_stride, rows):
+        c = self.cfg
+        return self.fn(c.head_dim, c.dtype_code, x, y, x_stride, y_stride, rows, raw_stream(self.device))
+
+    # gpu.mojo:303-310 argument order
+    def _unpack(self, grid, cache, bs, hs, hkv, page_blk, page_dst, n_pages, tail_blk, tail_info, n_tail, tail_k, k_new,
+                v_new, k_stride, v_stride, new_dst, n_new, kp, vp, rot):
+        c = self.cfg
+        return self.fn(c.head_dim, c.bits, c.page, c.dtype_code, cache, bs, hs, hkv, page_blk, page_dst, n_pages,
+                       tail_blk, tail_info, n_tail, tail_k, k_new, v_new, k_stride, v_stride, new_dst, n_new, kp, vp, rot,
+                       raw_stream(self.device))
+
+
+NAMES = ("append", "write", "decode", "combine", "fwht", "unpack")
+
+
+@lru_cache(None)
+def kernels(device: int, cfg: GpuConfig) -> dict[str, Kernel]:
+    """{name: Kernel} for one device and configuration (kushkash/_cuda.py:106-108)."""
+    return {name: Kernel(device, cfg, name) for name in NAMES}
+
+
+def arch(device: int) -> str:
+    major, minor = torch.cuda.get_device_capability(device)
+    return f"sm_{major}{minor}"
+
+
+def sm_count(device: int) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count

@@ -1,0 +1,157 @@
+// Shared definitions of the sm_100a kushkash kernels: the page-record format, the bit-exact quantizer arithmetic,
+// dtype helpers, template dispatch and the C-ABI error plumbing.
+//
+// Page record of one (page, kv head), P tokens, D channels, BITS in {4, 8} (kushkash/kush/quant.mojo:53-87):
+//   [ kq: P*DC int8 | vq: P*DC int8 | ks: D fp16 | kb: D fp16 | vs: P fp16 | vb: P fp16 ],  DC = D (int8) or D/2
+//   x ~= s * c + b, c in [-2^(BITS-1), 2^(BITS-1) - 1]; K: (s, b) per channel over the page, V: per token.
+//   int4 byte j of a row = code of dim j (low nibble) | code of dim j + D/2 (high nibble).
+// Record of (block b, kv head h) at cache + b*block_stride + h*head_stride (byte strides).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+#include <utility>
+
+#include "../../include/kushkash_b200.h"
+
+namespace kush {
+
+constexpr int WARP = 32;
+
+template <int D, int BITS, int P>
+struct Fmt {
+    static_assert(D == 64 || D == 128 || D == 256, "head_dim must be 64, 128 or 256");
+    static_assert(BITS == 4 || BITS == 8, "bits must be 4 or 8");
+    static_assert(P == 16 || P == 32, "page must be 16 or 32 tokens");
+    static constexpr int DC = BITS == 8 ? D : D / 2;          // bytes per token row
+    static constexpr int OFF_VQ = P * DC;
+    static constexpr int OFF_KS = 2 * P * DC;
+    static constexpr int OFF_KB = OFF_KS + 2 * D;
+    static constexpr int OFF_VS = OFF_KS + 4 * D;
+    static constexpr int OFF_VB = OFF_VS + 2 * P;
+    static constexpr int RB = 2 * P * DC + 4 * D + 4 * P;      // record bytes (a multiple of 16 for D % 64 == 0)
+    static constexpr int HALF = 1 << (BITS - 1);
+};
+
+// ------------------------------------------------------------------ dtypes
+template <class T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <class T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+__device__ __forceinline__ float h_load(const uint8_t* p, int i) {
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+__device__ __forceinline__ void h_store(uint8_t* p, int i, float v) { reinterpret_cast<__half*>(p)[i] = __float2half_rn(v); }
+
+// ------------------------------------------------------------------ quantizer (quant.mojo:25-50), bit-exact
+// Every operation is an explicitly rounded intrinsic so that no contraction can change a rounding: the pages must
+// equal the reference's byte for byte.
+template <int BITS>
+__device__ __forceinline__ void qparams(float mn, float mx, float& s, float& b, float& inv) {
+    constexpr float LEVELS = float((1 << BITS) - 1);
+    constexpr float HALFF = float(1 << (BITS - 1));
+    s = __half2float(__float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), LEVELS)));
+    b = __half2float(__float2half_rn(__fadd_rn(mn, __fmul_rn(s, HALFF))));
+    inv = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+}
+
+// round((x - b) * inv) with ties to even (torch.round, as the reference's tests pin), clamped to the code range
+template <int BITS>
+__device__ __forceinline__ int qcode(float x, float b, float inv) {
+    constexpr float HALFF = float(1 << (BITS - 1));
+    float r = rintf(__fmul_rn(__fsub_rn(x, b), inv));
+    r = fminf(fmaxf(r, -HALFF), HALFF - 1.0f);
+    return int(r);
+}
+
+__device__ __forceinline__ uint8_t pack4(int lo, int hi) { return uint8_t((lo & 0x0F) | ((hi & 0x0F) << 4)); }
+
+// code of dim c of one token row, as an int (int4: dim c < D/2 is the low nibble of byte c, else the high nibble of
+// byte c - D/2; two's complement)
+template <int D, int BITS>
+__device__ __forceinline__ int code_at(const uint8_t* row, int c) {
+    if constexpr (BITS == 8) {
+        return int(int8_t(row[c]));
+    } else {
+        int b = int(int8_t(row[c < D / 2 ? c : c - D / 2]));
+        return c < D / 2 ? ((b << 28) >> 28) : (b >> 4);
+    }
+}
+
+// ------------------------------------------------------------------ warp helpers
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+    return x;
+}
+__device__ __forceinline__ float warp_min(float x) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x = fminf(x, __shfl_xor_sync(0xffffffffu, x, o));
+    return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// ------------------------------------------------------------------ host-side dispatch
+template <int V> using IC = std::integral_constant<int, V>;
+
+template <class F> int dispatch_page(int page, F&& f) {
+    switch (page) {
+        case 16: return f(IC<16>{});
+        case 32: return f(IC<32>{});
+        default: return KUSH_ERR_UNSUPPORTED;
+    }
+}
+template <class F> int dispatch_bits(int bits, F&& f) {
+    switch (bits) {
+        case 4: return f(IC<4>{});
+        case 8: return f(IC<8>{});
+        default: return KUSH_ERR_UNSUPPORTED;
+    }
+}
+template <class F> int dispatch_dim(int d, F&& f) {
+    switch (d) {
+        case 64: return f(IC<64>{});
+        case 128: return f(IC<128>{});
+        case 256: return f(IC<256>{});
+        default: return KUSH_ERR_UNSUPPORTED;
+    }
+}
+template <class F> int dispatch_dtype(int dtype, F&& f) {
+    switch (dtype) {
+        case KUSH_F16: return f(__half{});
+        case KUSH_BF16: return f(__nv_bfloat16{});
+        case KUSH_F32: return f(float{});
+        default: return KUSH_ERR_UNSUPPORTED;
+    }
+}
+// (head_dim, bits, page, dtype) -> f(IC<D>, IC<BITS>, IC<P>, IN{})
+template <class F> int dispatch_fmt(int d, int bits, int page, int dtype, F&& f) {
+    return dispatch_dim(d, [&](auto D) {
+        return dispatch_bits(bits, [&](auto B) {
+            return dispatch_page(page, [&](auto P) { return dispatch_dtype(dtype, [&](auto in) { return f(D, B, P, in); }); });
+        });
+    });
+}
+
+// records the message of the last failed call on this host thread; returns the status to hand back
+int set_error(int status, const char* fmt, ...);
+// checks the launch that just happened (cudaGetLastError); KUSH_OK or KUSH_ERR_CUDA with the message recorded
+int check_launch(const char* what);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace kush

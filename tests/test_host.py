@@ -1,0 +1,95 @@
+"""Host-side logic on the CPU (no GPU): the C-ABI library loads and exports every entry point include/*.h declares,
+configuration checks, the split-KV heuristic, format helpers, and the product's refusal of a CPU device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_entry_points() -> list[str]:
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        names += re.findall(r"^\w[\w\s\*]*?\b(kush_sm100_\w+)\s*\(", h.read_text(), re.M)
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    from kushkash_b200._cuda import LIB_PATH, SIGNATURES, lib
+    names = declared_entry_points()
+    assert len(names) >= 10, names
+    dll = ctypes.CDLL(str(LIB_PATH))
+    for n in names:
+        assert hasattr(dll, n), f"{n} declared in include/ but not exported"
+        assert n in SIGNATURES, f"{n} has no ctypes signature in kushkash_b200/_cuda.py"
+    assert lib().kush_sm100_version().startswith(b"kushkash_b200")
+
+
+def test_record_bytes_agree():
+    from kushkash_b200._cuda import lib
+    from kushkash_b200 import record_bytes
+    from oracle.kush_oracle import record_bytes as oracle_rb
+    for D in (64, 128, 256):
+        for bits in (4, 8):
+            for P in (16, 32):
+                assert lib().kush_sm100_record_bytes(D, bits, P) == record_bytes(D, bits, P) == oracle_rb(D, bits, P)
+                assert record_bytes(D, bits, P) % 16 == 0
+    assert record_bytes(128, 4) == 4736 and record_bytes(128, 8) == 8832 and record_bytes(128, 4, 16) == 2624
+    assert lib().kush_sm100_record_bytes(96, 4, 32) == 0
+
+
+def test_unsupported_configuration_reports_error_without_gpu():
+    from kushkash_b200._cuda import KUSH_ERR_UNSUPPORTED, lib, last_error
+    rc = lib().kush_sm100_fwht(96, 1, ctypes.c_void_p(16), ctypes.c_void_p(16), 96, 96, 1, None)
+    assert rc == KUSH_ERR_UNSUPPORTED and "head_dim 96" in last_error()
+    assert lib().kush_sm100_decode_tensor_cores(96, 4, 32, 1, 4) == KUSH_ERR_UNSUPPORTED
+
+
+def test_gpu_config_validation():
+    from kushkash_b200 import BuildError, GpuConfig
+    GpuConfig(128, 4, 4, "bfloat16", "sm_100", 16)
+    for bad in ((96, 4, 4, "bfloat16", "sm_100"), (128, 3, 4, "bfloat16", "sm_100"),
+                (128, 4, 4, "float64", "sm_100"), (128, 4, 0, "bfloat16", "sm_100"),
+                (128, 4, 4, "bfloat16", "sm_90")):
+        with pytest.raises(BuildError):
+            GpuConfig(*bad)
+    with pytest.raises(BuildError):
+        GpuConfig(128, 4, 4, "bfloat16", "sm_100", 64)
+
+
+def test_ops_refuses_cpu_device():
+    from kushkash_b200 import Ops
+    with pytest.raises(ValueError, match="CUDA"):
+        Ops(torch.device("cpu"), 128, 4, 4, torch.float32)
+
+
+def test_split_factor():
+    from kushkash_b200._ops import split_factor
+    assert split_factor(256, 8, 256, 148) == 1                    # 2048 units already
+    assert split_factor(4, 8, 4096, 148) == 64                    # config 4, one GPU: 64 splits
+    assert split_factor(4, 1, 4096, 148) == 256                   # config 4, one kv head per GPU: capped at 256
+    assert split_factor(1, 1, 7, 148) == 1                        # too few pages to split
+    assert split_factor(1, 1, 16, 148) == 4                       # >= 4 pages per split
+    for S, H, n in ((1, 1, 10 ** 6), (3, 5, 999)):
+        ns = split_factor(S, H, n, 148)
+        assert ns & (ns - 1) == 0 and 1 <= ns <= 256
+
+
+def test_dequant_helpers_roundtrip_on_cpu():
+    """cached_kv over oracle-written pages reproduces the quantizer's dequantization (the host-side format view)."""
+    from kushkash_b200 import cached_kv
+    from kushsim import fill, make_state
+    from oracle.kush_oracle import OracleOps
+    for P in (16, 32):
+        B, H, D, n = 2, 2, 64, 3 * P + 3
+        g = torch.Generator().manual_seed(P)
+        K, V = torch.randn(B, H, n, D, generator=g), torch.randn(B, H, n, D, generator=g)
+        bt = torch.randperm(B * 4, generator=g).to(torch.int32).view(B, 4)
+        st = make_state(B, H, D, 8, P, bt, B * 4)
+        fill(OracleOps(D, 8, 1, P), st, K, V, n - 5, torch.float32, "cpu")
+        hk, hv = cached_kv(st.pool, st.block_table, n, st.tail_k, D, 8, torch.float32, P)
+        assert torch.equal(hk[:, :, n - n % P:], K[:, :, n - n % P:])         # exact tail
+        assert (hk - K).abs().max() < 0.05 and (hv - V).abs().max() < 0.05      # int8 pages
