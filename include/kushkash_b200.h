@@ -90,6 +90,11 @@ int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void *out
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);
 
+/* Bounded-wait watchdog of the decode kernels: 1 if a decode launch gave up waiting for a page copy (its outputs
+ * were written as NaN), else 0; clear != 0 resets the flag.  Synchronous (reads a device variable); -1 on a CUDA
+ * error.  No counterpart in the reference, whose kernels have no bounded waits. */
+int kush_sm100_device_error(int32_t clear);
+
 /* Canonical Walsh-Hadamard rotation of `rows` rows of head_dim values: y[r] = fwht(x[r]) (row strides in
  * elements; y may alias x).  Replaces kush_fwht (kushkash/kush/gpu.mojo:95-112) as launched by Ops.fwht
  * (kushkash/_ops.py:104-127): fp32 butterflies over strides 1, 2, ..., D/2 in that order, then one multiply by

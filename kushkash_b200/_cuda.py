@@ -38,6 +38,7 @@ SIGNATURES = {
     "kush_sm100_unpack": [_i32, _i32, _i32, _i32, _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _i64,
                           _i64, _p, _i32, _p, _p, _i32, _p],
     "kush_sm100_record_bytes": [_i32, _i32, _i32],
+    "kush_sm100_device_error": [_i32],
     "kush_sm100_last_error": [],
     "kush_sm100_version": [],
 }
@@ -73,6 +74,14 @@ def check(rc: int, what: str) -> None:
     if rc in (KUSH_ERR_UNSUPPORTED, KUSH_ERR_ARG):
         raise ValueError(f"launch {what}: {msg}")
     raise RuntimeError(f"launch {what}: {msg}")
+
+
+def device_error(clear: bool = True) -> int:
+    """1 if a decode launch gave up a bounded wait since the last clear (its outputs are NaN), else 0."""
+    rc = lib().kush_sm100_device_error(int(clear))
+    if rc < 0:
+        raise RuntimeError("kush_sm100_device_error: CUDA error")
+    return rc
 
 
 def raw_stream(device: int) -> int:

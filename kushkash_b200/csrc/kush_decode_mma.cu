@@ -1,14 +1,606 @@
-// Tensor-core decode kernel (placeholder until the mma kernel lands): no configuration selects it yet.
+// Fused dequant paged decode attention on the tensor cores (sm_100a), for fp16 / bf16 q and outputs.
+//
+// Same contract as the reference's kush_decode_tc (kushkash/kush/gpu.mojo:566-807); the algebra differs only in
+// where the K scale and bias enter (below), the rest -- page-granular online softmax, V scale folded into the
+// softmax weights and V bias into one scalar per head, exact-K tail, warp merge, split-KV partials -- is the same.
+//
+// Work split: grid (S, Hkv, n_splits), 4 warps per CTA.  Split z owns a contiguous page range; warp w takes pages
+// start + w, start + w + 4, ...  Each warp streams its pages through its own ring of NS shared-memory slots with
+// one 1-D bulk copy per page record (cp.async.bulk, completion on an mbarrier; no multicast), issued NS pages
+// ahead by lane 0, with the block-table entries prefetched 32 pages at a time into registers.  All waits are
+// bounded: on a timeout the kernel records an error flag, writes NaN outputs and returns.
+//
+// Per 16-token tile of a page, with m16n8k16 fp16 MMAs (fp32 accumulation):
+//   QK:  S^T[16 tok x 8 heads] = K'[16 tok x D] . Qh^T[D x 8 heads]     (tokens on M, heads on N)
+//        K' = c * ks + (kb - kb_ref) in fp16 (HFMA2), kb_ref = the K bias of the sequence's first page: the large
+//        per-channel offsets cancel before rounding, and the constant q . kb_ref shifts every score of (s, h)
+//        equally, which the softmax ignores (the exact-K tail subtracts it too).  Qh = fp16(q * scale * log2 e)
+//        is therefore constant for the whole CTA (B fragments loaded once); scores are in log2 units (exp2).
+//   PV:  O^T[16 dims x 8 heads] += V^T[16 dims x 16 tok] . P'^T[16 tok x 8 heads], P' = fp16(p * vs_t): the
+//        S^T accumulators become P' B fragments with one movmatrix.trans per 8x8 block.
+// Codes become exact fp16 with the magic-number trick (a code under the exponent of 1024, then one subtract);
+// the D dimension is permuted so every lane's fragments come from whole 32-bit words of its token rows.
+#include <stdio.h>
+
 #include "kush_common.cuh"
 
 namespace kush {
 
-int decode_mma_supported(int, int, int, int, int) { return 0; }
+constexpr int MMA_NW = 4;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;      // try_wait polls before a wait is declared stuck
 
-int launch_decode_mma(int, int, int, int, int, const void*, void*, const void*, int64_t, int64_t, const void*,
-                      const int32_t*, const int32_t*, const int32_t*, int64_t, int32_t, float, int32_t, float*, float*,
-                      int32_t, cudaStream_t) {
-    return set_error(KUSH_ERR_UNSUPPORTED, "tensor-core decode not built");
+__device__ int g_decode_error = 0;            // set when a bounded wait gave up (read by kush_sm100_device_error)
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+// (a & b) ^ c in one LOP3
+__device__ __forceinline__ uint32_t and_xor(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+    uint32_t r;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ float fast_exp2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait: false if the limit ran out
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < WAIT_LIMIT; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+// one 1-D bulk copy global -> shared (no multicast), completing `bytes` on `bar`
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// fp16 constants as f16x2 words
+constexpr uint32_t H2_1032 = 0x64086408u;       // 1024 + 8: int4 low-nibble offset
+constexpr uint32_t H2_1152 = 0x64806480u;       // 1024 + 128: int8 offset
+constexpr uint32_t H2_INV16 = 0x2C002C00u;      // 1/16
+constexpr uint32_t H2_M72 = 0xD480D480u;        // -72 = -(1024/16 + 8)
+
+// ------------------------------------------------------------------ layouts
+template <int D, int BITS>
+struct Lay {
+    static constexpr int DC = BITS == 8 ? D : D / 2;
+    static constexpr int CB = DC / 4;           // K: bytes of a token row per lane (quarter rows, lane % 4)
+    static constexpr int CW = CB / 4;           // K: 32-bit words of it
+    static constexpr int KT = D / 16;           // k-tiles of QK
+    static constexpr int NPAIR = 2 * KT;        // K: f16x2 registers per token row per lane
+    static constexpr int VB = DC / 8;           // V: bytes of a token row per lane (eighth rows, lane / 4)
+    static constexpr int MT = D / 16;           // m-tiles (16 output dims) of PV
+    // first of the two dims held by K pair e of lane quarter tid (pairs: e = 2 kt -> a0/a1/b0, 2 kt + 1 -> a2/a3/b1)
+    __device__ static int kdim(int tid, int e) {
+        if constexpr (BITS == 4) {
+            const int wi = e >> 2, sub = e & 3;
+            return tid * CB + 4 * wi + (sub & 1) * 2 + (sub >> 1) * (D / 2);
+        } else {
+            return tid * CB + 4 * (e >> 1) + 2 * (e & 1);
+        }
+    }
+    // output dim of PV fragment row r (0..15) in m-tile mt for lane group g (rows g and g + 8 of the tile)
+    __device__ static int vdim(int g, int mt, int hi) {
+        if constexpr (BITS == 4) return g * VB + mt + hi * (D / 2);
+        else return g * VB + mt + hi * MT;
+    }
+};
+
+// K token row (CB bytes at `row` for this lane) -> NPAIR f16x2 of K' = c * ks + dkb, in pair order
+template <int D, int BITS>
+__device__ __forceinline__ void k_pairs(const uint8_t* row, const uint32_t (&ks)[2 * (D / 16)],
+                                        const uint32_t (&dkb)[2 * (D / 16)], uint32_t (&out)[2 * (D / 16)]) {
+    using L = Lay<D, BITS>;
+    const uint4* src = reinterpret_cast<const uint4*>(row);
+    uint32_t w[L::CW];
+#pragma unroll
+    for (int i = 0; i < L::CW / 4; i++) {
+        const uint4 v = src[i];
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+    }
+    if constexpr (L::CW % 4 != 0) {             // D = 64 int4: 8 bytes per lane
+        const uint2 v = *reinterpret_cast<const uint2*>(row);
+        w[0] = v.x;
+        w[1] = v.y;
+    }
+#pragma unroll
+    for (int wi = 0; wi < L::CW; wi++) {
+        if constexpr (BITS == 4) {
+            const uint32_t x = prmt(w[wi], 0, 0x3120);          // bytes [b0, b2, b1, b3]
+            const uint32_t y = x >> 8;                          // bytes [b2, b1, b3, 0]
+            const uint32_t c0 = h2_sub(and_xor(x, 0x000F000Fu, H2_1032), H2_1032);            // lo (b0, b1)
+            const uint32_t c1 = h2_sub(and_xor(y, 0x000F000Fu, H2_1032), H2_1032);            // lo (b2, b3)
+            const uint32_t c2 = h2_fma(and_xor(x, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);  // hi (b0, b1)
+            const uint32_t c3 = h2_fma(and_xor(y, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);  // hi (b2, b3)
+            out[4 * wi] = h2_fma(c0, ks[4 * wi], dkb[4 * wi]);
+            out[4 * wi + 1] = h2_fma(c1, ks[4 * wi + 1], dkb[4 * wi + 1]);
+            out[4 * wi + 2] = h2_fma(c2, ks[4 * wi + 2], dkb[4 * wi + 2]);
+            out[4 * wi + 3] = h2_fma(c3, ks[4 * wi + 3], dkb[4 * wi + 3]);
+        } else {
+            const uint32_t u = w[wi] ^ 0x80808080u;             // signed code -> c + 128
+            const uint32_t c0 = h2_sub(prmt(u, 0x64646464u, 0x5140), H2_1152);                 // (b0, b1)
+            const uint32_t c1 = h2_sub(prmt(u, 0x64646464u, 0x7342), H2_1152);                 // (b2, b3)
+            out[2 * wi] = h2_fma(c0, ks[2 * wi], dkb[2 * wi]);
+            out[2 * wi + 1] = h2_fma(c1, ks[2 * wi + 1], dkb[2 * wi + 1]);
+        }
+    }
+}
+
+// V^T A fragments of one 16-token tile: lane group g reads VB bytes of token rows 2tid, 2tid+1, 2tid+8, 2tid+9;
+// a[mt][0..3] = (row g | row g+8) x (tokens 2tid,2tid+1 | 2tid+8,2tid+9), exact codes
+template <int D, int BITS>
+__device__ __forceinline__ void v_frags(const uint8_t* vq, int g, int tid, uint32_t (&a)[D / 16][4]) {
+    using L = Lay<D, BITS>;
+    constexpr int NWV = (L::VB + 3) / 4;        // 32-bit words per lane per row
+    uint32_t w[4][NWV];
+    const int rows[4] = {2 * tid, 2 * tid + 1, 2 * tid + 8, 2 * tid + 9};
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const uint8_t* p = vq + rows[r] * L::DC + g * L::VB;
+        if constexpr (L::VB == 4) {
+            w[r][0] = *reinterpret_cast<const uint32_t*>(p);
+        } else if constexpr (L::VB == 8) {
+            const uint2 v = *reinterpret_cast<const uint2*>(p);
+            w[r][0] = v.x;
+            w[r][1] = v.y;
+        } else {
+#pragma unroll
+            for (int i = 0; i < NWV / 4; i++) {
+                const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+                w[r][4 * i] = v.x;
+                w[r][4 * i + 1] = v.y;
+                w[r][4 * i + 2] = v.z;
+                w[r][4 * i + 3] = v.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < L::MT; mt++) {
+#pragma unroll
+        for (int pr = 0; pr < 2; pr++) {                       // token pair (2tid, 2tid+1) or (2tid+8, 2tid+9)
+            if constexpr (BITS == 4) {
+                const int j = mt, wi = j >> 2, jj = j & 3;
+                const uint32_t sel = jj | (jj << 4) | ((4 + jj) << 8) | ((4 + jj) << 12);
+                const uint32_t x = prmt(w[2 * pr][wi], w[2 * pr + 1][wi], sel);     // halves: byte j of t0, t1
+                a[mt][2 * pr] = h2_sub(and_xor(x, 0x000F000Fu, H2_1032), H2_1032);                 // row g
+                a[mt][2 * pr + 1] = h2_fma(and_xor(x, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);  // row g+8
+            } else {
+#pragma unroll
+                for (int hi = 0; hi < 2; hi++) {
+                    const int j = mt + hi * L::MT, wi = j >> 2, jj = j & 3;
+                    const uint32_t sel = jj | (jj << 4) | ((4 + jj) << 8) | ((4 + jj) << 12);
+                    const uint32_t x = prmt(w[2 * pr][wi], w[2 * pr + 1][wi], sel);
+                    a[mt][2 * pr + hi] = h2_sub(and_xor(x, 0x00FF00FFu, 0x64806480u), H2_1152);
+                }
+            }
+        }
+    }
+}
+
+template <int D, int BITS, int P>
+struct MmaCfg {
+    static constexpr int RB = Fmt<D, BITS, P>::RB;
+    static constexpr int NS = RB <= 3072 ? 6 : RB <= 6144 ? 4 : RB <= 10240 ? 3 : 2;   // ring slots per warp
+    static constexpr int RING = MMA_NW * NS * RB;
+};
+
+// grid (S, Hkv, n_splits), block 128
+template <int D, int BITS, int P, int NT, class IN>
+__global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
+    const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
+    int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
+    const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
+    float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o) {
+    using F = Fmt<D, BITS, P>;
+    using L = Lay<D, BITS>;
+    using C = MmaCfg<D, BITS, P>;
+    constexpr int NW = MMA_NW, NS = C::NS, KT = L::KT, MT = L::MT, MTT = P / 16;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* ring = smem;                                               // [NW][NS][RB], reused for the merge
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::RING);       // [NW][NS]
+    float* qsm = reinterpret_cast<float*>(bars + NW * NS);              // [G][D] q * scale * log2e (tail)
+    float* kbr = qsm + G * D;                                           // [D] kb_ref
+    const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
+    const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP, g = lane >> 2, tid = lane & 3;
+    const int64_t n = seq_lens[s];
+    const int tail_n = int(n % P);
+    const int64_t full = n / P;
+    const int64_t pps = (full + n_splits - 1) / n_splits;
+    const int64_t p0 = min(full, int64_t(z) * pps), p1 = min(full, p0 + pps);
+    const int32_t* bt = block_table + int64_t(s) * max_pages;
+    const int64_t qbase = (int64_t(s) * H + h) * G * D;
+    const uint8_t* hcache = cache + int64_t(h) * head_stride;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NW * NS; i++) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm_log2;
+    // kb_ref: K bias of the sequence's first page (only when one is full; a tail-only sequence uses 0)
+    const uint8_t* rec0 = full > 0 ? hcache + int64_t(bt[0]) * block_stride : nullptr;
+    for (int i = threadIdx.x; i < D; i += NW * WARP) kbr[i] = rec0 ? h_load(rec0 + F::OFF_KB, i) : 0.0f;
+    __syncthreads();
+
+    // my pages: p0 + wid + i * NW, i < npw
+    const int64_t mine0 = p0 + wid;
+    const int npw = mine0 < p1 ? int((p1 - mine0 + NW - 1) / NW) : 0;
+    uint8_t* wring = ring + wid * NS * C::RB;
+    uint64_t* wbar = bars + wid * NS;
+    auto bt_at = [&](int i) -> int32_t { return i < npw ? bt[mine0 + int64_t(i) * NW] : 0; };
+    int32_t btw = bt_at(lane), btn = bt_at(32 + lane);                 // block ids of my pages, 32 at a time
+    auto issue = [&](int i, int32_t blk) {                              // lane 0: page i -> slot i % NS
+        if (lane == 0) {
+            uint64_t* bar = &wbar[i % NS];
+            fence_proxy_async();
+            mbar_expect_tx(bar, C::RB);
+            bulk_load(wring + (i % NS) * C::RB, hcache + int64_t(blk) * block_stride, C::RB, bar);
+        }
+    };
+#pragma unroll 1
+    for (int i = 0; i < NS && i < npw; i++) issue(i, __shfl_sync(0xffffffffu, btw, i));
+
+    // B fragments: Qh^T for heads nt*8 + g at this lane's K pairs; kb_ref pairs
+    uint32_t bq[NT][2 * KT];
+    uint32_t kref[2 * KT];
+#pragma unroll
+    for (int e = 0; e < 2 * KT; e++) {
+        const int d = L::kdim(tid, e);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int head = nt * 8 + g;
+            bq[nt][e] = head < G ? pack_h2(qsm[head * D + d], qsm[head * D + d + 1]) : 0u;
+        }
+        kref[e] = pack_h2(kbr[d], kbr[d + 1]);
+    }
+
+    float o[MT][NT][4];                                                  // O^T accumulators
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) o[mt][nt][k] = 0.0f;
+    float m[NT][2], l[NT][2], vbacc[NT][2];                              // heads nt*8 + 2tid + {0,1} (lane partials)
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            m[nt][e] = -INFINITY;
+            l[nt][e] = 0.0f;
+            vbacc[nt][e] = 0.0f;
+        }
+    bool ok = true;
+    int fail_at = npw;
+
+#pragma unroll 1
+    for (int i = 0; i < npw; i++) {
+        const int slot = i % NS;
+        if (!mbar_wait(&wbar[slot], uint32_t(i / NS) & 1u)) {
+            ok = false;
+            fail_at = i;
+            break;
+        }
+        const uint8_t* rec = wring + slot * C::RB;
+        // per-page K scale and bias pairs for this lane's dims (K' = c * ks + (kb - kb_ref))
+        uint32_t ks[2 * KT], dkb[2 * KT];
+#pragma unroll
+        for (int e = 0; e < 2 * KT; e++) {
+            const int d = L::kdim(tid, e);
+            ks[e] = *reinterpret_cast<const uint32_t*>(rec + F::OFF_KS + 2 * d);
+            dkb[e] = h2_sub(*reinterpret_cast<const uint32_t*>(rec + F::OFF_KB + 2 * d), kref[e]);
+        }
+        float sc[MTT][NT][4];
+#pragma unroll
+        for (int mtt = 0; mtt < MTT; mtt++) {
+            uint32_t ka[2 * KT], kb[2 * KT];                              // rows g and g + 8 of this 16-token tile
+            k_pairs<D, BITS>(rec + (mtt * 16 + g) * F::DC + tid * L::CB, ks, dkb, ka);
+            k_pairs<D, BITS>(rec + (mtt * 16 + g + 8) * F::DC + tid * L::CB, ks, dkb, kb);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                sc[mtt][nt][0] = sc[mtt][nt][1] = sc[mtt][nt][2] = sc[mtt][nt][3] = 0.0f;
+#pragma unroll
+                for (int kt = 0; kt < KT; kt++)
+                    mma16816(sc[mtt][nt], ka[2 * kt], kb[2 * kt], ka[2 * kt + 1], kb[2 * kt + 1], bq[nt][2 * kt],
+                             bq[nt][2 * kt + 1]);
+            }
+        }
+        // page-granular online softmax; lane holds tokens mtt*16 + g (+8), heads nt*8 + 2tid + {0,1}
+        float vsv[MTT][2], vbv[MTT][2];
+#pragma unroll
+        for (int mtt = 0; mtt < MTT; mtt++)
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                vsv[mtt][r] = h_load(rec + F::OFF_VS, mtt * 16 + g + 8 * r);
+                vbv[mtt][r] = h_load(rec + F::OFF_VB, mtt * 16 + g + 8 * r);
+            }
+        uint32_t pb[MTT][NT][2];                                          // P'^T B fragments per 16-token tile
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int mtt = 0; mtt < MTT; mtt++) {
+                mx[0] = fmaxf(mx[0], fmaxf(sc[mtt][nt][0], sc[mtt][nt][2]));
+                mx[1] = fmaxf(mx[1], fmaxf(sc[mtt][nt][1], sc[mtt][nt][3]));
+            }
+            float corr[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], off));
+                const float mn = fmaxf(m[nt][e], mx[e]);
+                corr[e] = fast_exp2(m[nt][e] - mn);
+                m[nt][e] = mn;
+                l[nt][e] *= corr[e];
+                vbacc[nt][e] *= corr[e];
+            }
+#pragma unroll
+            for (int mtt = 0; mtt < MTT; mtt++) {
+                float pv[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int e = k & 1, r = k >> 1;
+                    const float p = fast_exp2(sc[mtt][nt][k] - m[nt][e]);
+                    l[nt][e] += p;
+                    vbacc[nt][e] += p * vbv[mtt][r];
+                    pv[k] = p * vsv[mtt][r];
+                }
+                pb[mtt][nt][0] = movmatrix_t(pack_h2(pv[0], pv[1]));       // tokens 0-7 of the tile
+                pb[mtt][nt][1] = movmatrix_t(pack_h2(pv[2], pv[3]));       // tokens 8-15
+            }
+            if (corr[0] != 1.0f || corr[1] != 1.0f) {
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++) {
+                    o[mt][nt][0] *= corr[0];
+                    o[mt][nt][1] *= corr[1];
+                    o[mt][nt][2] *= corr[0];
+                    o[mt][nt][3] *= corr[1];
+                }
+            }
+        }
+        // PV
+#pragma unroll
+        for (int mtt = 0; mtt < MTT; mtt++) {
+            uint32_t va[MT][4];
+            v_frags<D, BITS>(rec + F::OFF_VQ + mtt * 16 * F::DC, g, tid, va);
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++)
+                    mma16816(o[mt][nt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb[mtt][nt][0], pb[mtt][nt][1]);
+        }
+        __syncwarp();
+        // refill this slot with page i + NS
+        const int j = i + NS;
+        if (j < npw) {
+            if ((j & 31) == 0) {
+                btw = btn;
+                btn = bt_at(j + 32 + lane);
+            }
+            issue(j, __shfl_sync(0xffffffffu, btw, j & 31));
+        }
+    }
+    if (!ok) {
+        // a copy never completed: record it, wait (bounded) for this warp's copies still in flight, produce NaN
+        if (lane == 0) atomicExch(&g_decode_error, 1);
+        for (int i = fail_at + 1; i < fail_at + NS && i < npw; i++) mbar_wait(&wbar[i % NS], uint32_t(i / NS) & 1u);
+    }
+    ok = __syncthreads_and(ok);
+
+    // merge (kushkash/kush/gpu.mojo:438-466): per warp m, l, O + vbacc -> shared; partial NW = the exact-K tail
+    float* c_acc = reinterpret_cast<float*>(ring);                        // [NW + 1][G][D]
+    float* c_m = c_acc + (NW + 1) * G * D;                                // [NW + 1][G]
+    float* c_l = c_m + (NW + 1) * G;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                l[nt][e] += __shfl_xor_sync(0xffffffffu, l[nt][e], off);
+                vbacc[nt][e] += __shfl_xor_sync(0xffffffffu, vbacc[nt][e], off);
+            }
+        }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int head = nt * 8 + 2 * tid + e;
+            if (head < G) {
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++) {
+                    c_acc[(wid * G + head) * D + L::vdim(g, mt, 0)] = o[mt][nt][e] + vbacc[nt][e];
+                    c_acc[(wid * G + head) * D + L::vdim(g, mt, 1)] = o[mt][nt][2 + e] + vbacc[nt][e];
+                }
+                if (g == 0) {
+                    c_m[wid * G + head] = m[nt][e];
+                    c_l[wid * G + head] = l[nt][e];
+                }
+            }
+        }
+    // the tail page: exact K from tail_k, V rows from its record; warp 0, fp32 on the CUDA cores
+    if (wid == 0) {
+        const bool has_tail = tail_n > 0 && z == n_splits - 1;
+        for (int hd = 0; hd < G; hd++) {
+            float x = -INFINITY;
+            if (has_tail && lane < tail_n) {
+                const IN* tk = tail_k + ((int64_t(tail_idx[s]) * H + h) * P + lane) * D;
+                float acc = 0.0f;
+                for (int d = 0; d < D; d++) acc += qsm[hd * D + d] * (to_f32(tk[d]) - kbr[d]);
+                x = acc;
+            }
+            const float mx = warp_max(x);
+            const float p = (has_tail && lane < tail_n) ? fast_exp2(x - mx) : 0.0f;
+            const float lsum = warp_sum(p);
+            if (lane == 0) {
+                c_m[NW * G + hd] = has_tail ? mx : -INFINITY;
+                c_l[NW * G + hd] = lsum;
+            }
+            const uint8_t* trec = has_tail ? hcache + int64_t(bt[full]) * block_stride : nullptr;
+            for (int d = lane; d < D; d += WARP) {
+                float acc = 0.0f;
+                for (int t = 0; t < tail_n && has_tail; t++) {
+                    const float pt = __shfl_sync(0xffffffffu, p, t);
+                    const float c = float(code_at<D, BITS>(trec + F::OFF_VQ + t * F::DC, d));
+                    acc += pt * (c * h_load(trec + F::OFF_VS, t) + h_load(trec + F::OFF_VB, t));
+                }
+                c_acc[(NW * G + hd) * D + d] = acc;
+            }
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += NW * WARP) {
+        const int hd = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int w = 0; w <= NW; w++) M = fmaxf(M, c_m[w * G + hd]);
+        float Ls = 0.0f, acc = 0.0f;
+        if (M > -INFINITY) {
+            for (int w = 0; w <= NW; w++) {
+                const float mw = c_m[w * G + hd];
+                if (mw > -INFINITY) {
+                    const float f = fast_exp2(mw - M);
+                    Ls += c_l[w * G + hd] * f;
+                    acc += f * c_acc[(w * G + hd) * D + d];
+                }
+            }
+        }
+        if (!ok) acc = NAN;
+        if (n_splits == 1) {
+            out[qbase + idx] = from_f32<IN>(Ls > 0.0f ? acc / Ls : (ok ? 0.0f : NAN));
+        } else {
+            const int64_t pb = ((int64_t(s) * H + h) * n_splits + z) * G + hd;
+            part_o[pb * D + d] = acc;
+            if (d == 0) {
+                part_ml[pb * 2] = M * 0.69314718055994531f;           // log2 units -> natural, for the combine
+                part_ml[pb * 2 + 1] = Ls;
+            }
+        }
+    }
+}
+
+template <int D, int BITS, int P, int NT, class IN>
+int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
+               const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
+               int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
+               int32_t n_seqs, cudaStream_t stream) {
+    using C = MmaCfg<D, BITS, P>;
+    const size_t merge = sizeof(float) * (size_t(MMA_NW + 1) * G * D + 2 * size_t(MMA_NW + 1) * G);
+    const size_t ring = C::RING > merge ? size_t(C::RING) : (merge + 127) / 128 * 128;
+    const size_t smem = ring + sizeof(uint64_t) * MMA_NW * C::NS + sizeof(float) * (size_t(G) * D + D);
+    auto kern = decode_mma_kernel<D, BITS, P, NT, IN>;
+    if (ring != size_t(C::RING)) return set_error(KUSH_ERR_UNSUPPORTED, "decode: group %d too large for the ring", G);
+    static unsigned long long attr_set = 0;             // one bit per device: the attribute is per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_set >> (dev & 63) & 1ull)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "decode: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        attr_set |= 1ull << (dev & 63);
+    }
+    dim3 grid(n_seqs, hkv, n_splits);
+    kern<<<grid, MMA_NW * WARP, smem, stream>>>(static_cast<const IN*>(q), static_cast<IN*>(out),
+                                                static_cast<const uint8_t*>(cache), block_stride, head_stride,
+                                                static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens,
+                                                max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml,
+                                                part_o);
+    return check_launch("kush_sm100_decode (tensor cores)");
+}
+
+int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
+    if (dtype != KUSH_F16 && dtype != KUSH_BF16) return 0;
+    if ((D != 64 && D != 128 && D != 256) || (bits != 4 && bits != 8) || (P != 16 && P != 32)) return 0;
+    return G >= 1 && G <= (D == 256 ? 8 : 16);
+}
+
+int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
+                      int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
+                      const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
+                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, cudaStream_t stream) {
+    auto go = [&](auto Dc, auto Bc, auto Pc, auto in) -> int {
+        using IN = decltype(in);
+        if constexpr (std::is_same_v<IN, float>) {
+            return KUSH_ERR_UNSUPPORTED;
+        } else if constexpr (Dc.value == 256) {
+            return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
+                                                                   tail_idx, block_table, seq_lens, max_pages, hkv,
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, stream);
+        } else {
+            if (G <= 8)
+                return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride,
+                                                                       tail_k, tail_idx, block_table, seq_lens,
+                                                                       max_pages, hkv, scale, n_splits, part_ml,
+                                                                       part_o, n_seqs, stream);
+            return launch_mma<Dc.value, Bc.value, Pc.value, 2, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
+                                                                   tail_idx, block_table, seq_lens, max_pages, hkv,
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, stream);
+        }
+    };
+    return dispatch_fmt(D, bits, P, dtype, go);
 }
 
 }  // namespace kush
+
+extern "C" int kush_sm100_device_error(int32_t clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, kush::g_decode_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear && v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(kush::g_decode_error, &zero, sizeof(int));
+    }
+    return v;
+}
