@@ -73,6 +73,8 @@ extern "C" int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, i
     if (!aligned16(cache) || (block_stride & 15) || (head_stride & 15))
         return set_error(KUSH_ERR_ARG, "kush_sm100_decode: records must be 16-byte aligned (cache %p, strides %lld %lld)",
                          cache, (long long)block_stride, (long long)head_stride);
+    if (!aligned16(tail_k) || !aligned16(q) || !aligned16(out))
+        return set_error(KUSH_ERR_ARG, "kush_sm100_decode: q, out and tail_k must be 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (decode_mma_supported(head_dim, bits, page, dtype, group))
         return launch_decode_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,

@@ -79,32 +79,30 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// bounded wait: false if the limit ran out
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++)
-        if (mbar_try_wait(bar, parity)) return true;
+// bounded wait on the mbarrier at shared address `bar` for phase parity `parity`
+__device__ __forceinline__ bool mbar_wait_u32(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
     return false;
 }
-// one 1-D bulk copy global -> shared (no multicast), completing `bytes` on `bar`
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
+// lane 0 of the warp (predicated, no branch): arm `bar` for `bytes` and start one 1-D bulk copy src -> dst (shared
+// addresses).  The slot's previous contents were read into registers and consumed by MMAs before this point in
+// program order, so no proxy fence is needed between those reads and the async-proxy write.
+__device__ __forceinline__ void refill_lane0(uint32_t lane, uint32_t bar, uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.eq.u32 p, %0, 0;\n"
+        " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %3;\n"
+        " @p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%4], %3, [%1];\n}\n" ::"r"(lane),
+        "r"(bar), "r"(dst), "r"(bytes), "l"(src)
+        : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
 // fp16 constants as f16x2 words
@@ -139,45 +137,85 @@ struct Lay {
     }
 };
 
-// K token row (CB bytes at `row` for this lane) -> NPAIR f16x2 of K' = c * ks + dkb, in pair order
+// this lane's scale (or bias) pairs of one page, in K pair order, with 16-byte loads from the record in shared
+// memory.  int4: pair e = 4 wi + sub covers dims run[sub >> 1] + 2 (2 wi + (sub & 1)), two runs of CB dims (one in
+// each half of D); int8: pair e covers dims tid * CB + 2 e, one run of CB dims.
 template <int D, int BITS>
-__device__ __forceinline__ void k_pairs(const uint8_t* row, const uint32_t (&ks)[2 * (D / 16)],
-                                        const uint32_t (&dkb)[2 * (D / 16)], uint32_t (&out)[2 * (D / 16)]) {
+__device__ __forceinline__ void load_pairs(const uint8_t* arr, int tid, uint32_t (&out)[2 * (D / 16)]) {
     using L = Lay<D, BITS>;
-    const uint4* src = reinterpret_cast<const uint4*>(row);
-    uint32_t w[L::CW];
+    constexpr int RUNS = BITS == 4 ? 2 : 1;
+    constexpr int RW = L::CB / 2;                              // words per run
+    uint32_t run[RUNS][RW];
 #pragma unroll
-    for (int i = 0; i < L::CW / 4; i++) {
-        const uint4 v = src[i];
-        w[4 * i] = v.x;
-        w[4 * i + 1] = v.y;
-        w[4 * i + 2] = v.z;
-        w[4 * i + 3] = v.w;
+    for (int h = 0; h < RUNS; h++) {
+        const uint4* src = reinterpret_cast<const uint4*>(arr + 2 * (tid * L::CB + h * (D / 2)));
+#pragma unroll
+        for (int i = 0; i < RW / 4; i++) {
+            const uint4 v = src[i];
+            run[h][4 * i] = v.x;
+            run[h][4 * i + 1] = v.y;
+            run[h][4 * i + 2] = v.z;
+            run[h][4 * i + 3] = v.w;
+        }
     }
-    if constexpr (L::CW % 4 != 0) {             // D = 64 int4: 8 bytes per lane
-        const uint2 v = *reinterpret_cast<const uint2*>(row);
-        w[0] = v.x;
-        w[1] = v.y;
+#pragma unroll
+    for (int e = 0; e < 2 * L::KT; e++) {
+        if constexpr (BITS == 4) out[e] = run[(e & 3) >> 1][2 * (e >> 2) + (e & 1)];
+        else out[e] = run[0][e];
+    }
+}
+
+// K' = c * ks + dkb of token rows g (row0) and g + 8 (row1) of a 16-token tile, straight into m16n8k16 A-fragment
+// order: a[kt] = {row g pair 2kt, row g+8 pair 2kt, row g pair 2kt+1, row g+8 pair 2kt+1} (pair order of Lay::kdim)
+template <int D, int BITS>
+__device__ __forceinline__ void k_frags(const uint8_t* row0, const uint8_t* row1, const uint32_t (&ks)[2 * (D / 16)],
+                                        const uint32_t (&dkb)[2 * (D / 16)], uint32_t (&a)[D / 16][4]) {
+    using L = Lay<D, BITS>;
+    uint32_t w[2][L::CW];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint8_t* row = r ? row1 : row0;
+        if constexpr (L::CW % 4 != 0) {                        // D = 64 int4: 8 bytes per lane
+            const uint2 v = *reinterpret_cast<const uint2*>(row);
+            w[r][0] = v.x;
+            w[r][1] = v.y;
+        } else {
+            const uint4* src = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+            for (int i = 0; i < L::CW / 4; i++) {
+                const uint4 v = src[i];
+                w[r][4 * i] = v.x;
+                w[r][4 * i + 1] = v.y;
+                w[r][4 * i + 2] = v.z;
+                w[r][4 * i + 3] = v.w;
+            }
+        }
     }
 #pragma unroll
     for (int wi = 0; wi < L::CW; wi++) {
-        if constexpr (BITS == 4) {
-            const uint32_t x = prmt(w[wi], 0, 0x3120);          // bytes [b0, b2, b1, b3]
-            const uint32_t y = x >> 8;                          // bytes [b2, b1, b3, 0]
-            const uint32_t c0 = h2_sub(and_xor(x, 0x000F000Fu, H2_1032), H2_1032);            // lo (b0, b1)
-            const uint32_t c1 = h2_sub(and_xor(y, 0x000F000Fu, H2_1032), H2_1032);            // lo (b2, b3)
-            const uint32_t c2 = h2_fma(and_xor(x, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);  // hi (b0, b1)
-            const uint32_t c3 = h2_fma(and_xor(y, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);  // hi (b2, b3)
-            out[4 * wi] = h2_fma(c0, ks[4 * wi], dkb[4 * wi]);
-            out[4 * wi + 1] = h2_fma(c1, ks[4 * wi + 1], dkb[4 * wi + 1]);
-            out[4 * wi + 2] = h2_fma(c2, ks[4 * wi + 2], dkb[4 * wi + 2]);
-            out[4 * wi + 3] = h2_fma(c3, ks[4 * wi + 3], dkb[4 * wi + 3]);
-        } else {
-            const uint32_t u = w[wi] ^ 0x80808080u;             // signed code -> c + 128
-            const uint32_t c0 = h2_sub(prmt(u, 0x64646464u, 0x5140), H2_1152);                 // (b0, b1)
-            const uint32_t c1 = h2_sub(prmt(u, 0x64646464u, 0x7342), H2_1152);                 // (b2, b3)
-            out[2 * wi] = h2_fma(c0, ks[2 * wi], dkb[2 * wi]);
-            out[2 * wi + 1] = h2_fma(c1, ks[2 * wi + 1], dkb[2 * wi + 1]);
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            if constexpr (BITS == 4) {
+                // pairs e = 4 wi + sub: sub 0 lo(b0,b1), 1 lo(b2,b3), 2 hi(b0,b1), 3 hi(b2,b3); kt = e >> 1
+                const uint32_t x = prmt(w[r][wi], 0, 0x3120);      // bytes [b0, b2, b1, b3]
+                const uint32_t y = x >> 8;                          // bytes [b2, b1, b3, 0]
+                const int e = 4 * wi;
+                const uint32_t c0 = h2_sub(and_xor(x, 0x000F000Fu, H2_1032), H2_1032);
+                const uint32_t c1 = h2_sub(and_xor(y, 0x000F000Fu, H2_1032), H2_1032);
+                const uint32_t c2 = h2_fma(and_xor(x, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);
+                const uint32_t c3 = h2_fma(and_xor(y, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);
+                a[2 * wi][r] = h2_fma(c0, ks[e], dkb[e]);
+                a[2 * wi][2 + r] = h2_fma(c1, ks[e + 1], dkb[e + 1]);
+                a[2 * wi + 1][r] = h2_fma(c2, ks[e + 2], dkb[e + 2]);
+                a[2 * wi + 1][2 + r] = h2_fma(c3, ks[e + 3], dkb[e + 3]);
+            } else {
+                // pairs e = 2 wi + sub: (b0,b1), (b2,b3); kt = wi
+                const uint32_t u = w[r][wi] ^ 0x80808080u;          // signed code -> c + 128
+                const uint32_t c0 = h2_sub(prmt(u, 0x64646464u, 0x5140), H2_1152);
+                const uint32_t c1 = h2_sub(prmt(u, 0x64646464u, 0x7342), H2_1152);
+                a[wi][r] = h2_fma(c0, ks[2 * wi], dkb[2 * wi]);
+                a[wi][2 + r] = h2_fma(c1, ks[2 * wi + 1], dkb[2 * wi + 1]);
+            }
         }
     }
 }
@@ -189,10 +227,9 @@ __device__ __forceinline__ void v_frags(const uint8_t* vq, int g, int tid, uint3
     using L = Lay<D, BITS>;
     constexpr int NWV = (L::VB + 3) / 4;        // 32-bit words per lane per row
     uint32_t w[4][NWV];
-    const int rows[4] = {2 * tid, 2 * tid + 1, 2 * tid + 8, 2 * tid + 9};
 #pragma unroll
     for (int r = 0; r < 4; r++) {
-        const uint8_t* p = vq + rows[r] * L::DC + g * L::VB;
+        const uint8_t* p = vq + (2 * tid + (r & 1) + 8 * (r >> 1)) * L::DC + g * L::VB;
         if constexpr (L::VB == 4) {
             w[r][0] = *reinterpret_cast<const uint32_t*>(p);
         } else if constexpr (L::VB == 8) {
@@ -233,28 +270,40 @@ __device__ __forceinline__ void v_frags(const uint8_t* vq, int g, int tid, uint3
     }
 }
 
-template <int D, int BITS, int P>
+template <int D, int BITS, int P, int NT>
 struct MmaCfg {
     static constexpr int RB = Fmt<D, BITS, P>::RB;
-    static constexpr int NS = RB <= 3072 ? 6 : RB <= 6144 ? 4 : RB <= 10240 ? 3 : 2;   // ring slots per warp
-    static constexpr int RING = MMA_NW * NS * RB;
+    // ring slots per warp: deep enough to keep ~2 pages in flight per warp at 4 CTAs per SM
+    static constexpr int NS = RB <= 3072 ? 4 : 2;
+    static constexpr int GMAX = 8 * NT;
+    static constexpr int MERGE = 4 * ((MMA_NW + 1) * GMAX * D + 2 * (MMA_NW + 1) * GMAX);
+    static constexpr int RING = MMA_NW * NS * RB > MERGE ? MMA_NW * NS * RB : (MERGE + 127) / 128 * 128;
+    static constexpr int BARS = (8 * MMA_NW * NS + 127) / 128 * 128;
+    // shared memory: [bars | ring (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D])]
+    static constexpr int SMEM = BARS + RING + 4 * (GMAX * D + D);
+    // CTAs per SM the register budget targets (the larger tiles need more registers per thread)
+    static constexpr int MINB = (D == 64 || (D == 128 && P == 16 && NT == 1)) ? 4 : NT == 1 && D == 128 ? 3 : 2;
 };
+
+// scores more than 2^TAU above the running max trigger a rescale; below that the stale max is kept (weights
+// p = exp2(s - m) <= 2^TAU stay far from fp16 overflow in p * vs)
+constexpr float TAU = 4.0f;
 
 // grid (S, Hkv, n_splits), block 128
 template <int D, int BITS, int P, int NT, class IN>
-__global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
+__global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB)) decode_mma_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
     float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o) {
     using F = Fmt<D, BITS, P>;
     using L = Lay<D, BITS>;
-    using C = MmaCfg<D, BITS, P>;
+    using C = MmaCfg<D, BITS, P, NT>;
     constexpr int NW = MMA_NW, NS = C::NS, KT = L::KT, MT = L::MT, MTT = P / 16;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* ring = smem;                                               // [NW][NS][RB], reused for the merge
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::RING);       // [NW][NS]
-    float* qsm = reinterpret_cast<float*>(bars + NW * NS);              // [G][D] q * scale * log2e (tail)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // [NW][NS]
+    uint8_t* ring = smem + C::BARS;                                     // [NW][NS][RB], reused for the merge
+    float* qsm = reinterpret_cast<float*>(ring + C::RING);              // [G][D] q * scale * log2e
     float* kbr = qsm + G * D;                                           // [D] kb_ref
     const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
     const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP, g = lane >> 2, tid = lane & 3;
@@ -271,29 +320,28 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
         for (int i = 0; i < NW * NS; i++) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
-    for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm_log2;
-    // kb_ref: K bias of the sequence's first page (only when one is full; a tail-only sequence uses 0)
-    const uint8_t* rec0 = full > 0 ? hcache + int64_t(bt[0]) * block_stride : nullptr;
-    for (int i = threadIdx.x; i < D; i += NW * WARP) kbr[i] = rec0 ? h_load(rec0 + F::OFF_KB, i) : 0.0f;
-    __syncthreads();
-
-    // my pages: p0 + wid + i * NW, i < npw
+    // my pages: p0 + wid + i * NW, i < npw; start their copies before anything else
     const int64_t mine0 = p0 + wid;
     const int npw = mine0 < p1 ? int((p1 - mine0 + NW - 1) / NW) : 0;
     uint8_t* wring = ring + wid * NS * C::RB;
     uint64_t* wbar = bars + wid * NS;
     auto bt_at = [&](int i) -> int32_t { return i < npw ? bt[mine0 + int64_t(i) * NW] : 0; };
     int32_t btw = bt_at(lane), btn = bt_at(32 + lane);                 // block ids of my pages, 32 at a time
+    const uint32_t ring_u = smem_u32(wring), bar_u = smem_u32(wbar);
     auto issue = [&](int i, int32_t blk) {                              // lane 0: page i -> slot i % NS
-        if (lane == 0) {
-            uint64_t* bar = &wbar[i % NS];
-            fence_proxy_async();
-            mbar_expect_tx(bar, C::RB);
-            bulk_load(wring + (i % NS) * C::RB, hcache + int64_t(blk) * block_stride, C::RB, bar);
-        }
+        const uint32_t slot = uint32_t(i) % NS;
+        refill_lane0(uint32_t(lane), bar_u + 8 * slot, ring_u + slot * C::RB, hcache + int64_t(blk) * block_stride,
+                     C::RB);
     };
+    __syncthreads();                                                    // barriers initialised
 #pragma unroll 1
     for (int i = 0; i < NS && i < npw; i++) issue(i, __shfl_sync(0xffffffffu, btw, i));
+
+    for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm_log2;
+    // kb_ref: K bias of the sequence's first page (only when one is full; a tail-only sequence uses 0)
+    const uint8_t* rec0 = full > 0 ? hcache + int64_t(bt[0]) * block_stride : nullptr;
+    for (int i = threadIdx.x; i < D; i += NW * WARP) kbr[i] = rec0 ? h_load(rec0 + F::OFF_KB, i) : 0.0f;
+    __syncthreads();
 
     // B fragments: Qh^T for heads nt*8 + g at this lane's K pairs; kb_ref pairs
     uint32_t bq[NT][2 * KT];
@@ -330,8 +378,8 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
 
 #pragma unroll 1
     for (int i = 0; i < npw; i++) {
-        const int slot = i % NS;
-        if (!mbar_wait(&wbar[slot], uint32_t(i / NS) & 1u)) {
+        const int slot = int(uint32_t(i) % NS);
+        if (!mbar_wait_u32(bar_u + 8 * slot, (uint32_t(i) / NS) & 1u)) {
             ok = false;
             fail_at = i;
             break;
@@ -339,71 +387,57 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
         const uint8_t* rec = wring + slot * C::RB;
         // per-page K scale and bias pairs for this lane's dims (K' = c * ks + (kb - kb_ref))
         uint32_t ks[2 * KT], dkb[2 * KT];
+        load_pairs<D, BITS>(rec + F::OFF_KS, tid, ks);
+        load_pairs<D, BITS>(rec + F::OFF_KB, tid, dkb);
 #pragma unroll
-        for (int e = 0; e < 2 * KT; e++) {
-            const int d = L::kdim(tid, e);
-            ks[e] = *reinterpret_cast<const uint32_t*>(rec + F::OFF_KS + 2 * d);
-            dkb[e] = h2_sub(*reinterpret_cast<const uint32_t*>(rec + F::OFF_KB + 2 * d), kref[e]);
-        }
+        for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref[e]);
         float sc[MTT][NT][4];
 #pragma unroll
         for (int mtt = 0; mtt < MTT; mtt++) {
-            uint32_t ka[2 * KT], kb[2 * KT];                              // rows g and g + 8 of this 16-token tile
-            k_pairs<D, BITS>(rec + (mtt * 16 + g) * F::DC + tid * L::CB, ks, dkb, ka);
-            k_pairs<D, BITS>(rec + (mtt * 16 + g + 8) * F::DC + tid * L::CB, ks, dkb, kb);
+            uint32_t ka[KT][4];                                           // A fragments of this 16-token tile
+            const uint8_t* r0 = rec + (mtt * 16 + g) * F::DC + tid * L::CB;
+            k_frags<D, BITS>(r0, r0 + 8 * F::DC, ks, dkb, ka);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                sc[mtt][nt][0] = sc[mtt][nt][1] = sc[mtt][nt][2] = sc[mtt][nt][3] = 0.0f;
+                float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // two chains
 #pragma unroll
-                for (int kt = 0; kt < KT; kt++)
-                    mma16816(sc[mtt][nt], ka[2 * kt], kb[2 * kt], ka[2 * kt + 1], kb[2 * kt + 1], bq[nt][2 * kt],
-                             bq[nt][2 * kt + 1]);
+                for (int kt = 0; kt < KT; kt += 2) {
+                    mma16816(s0, ka[kt][0], ka[kt][1], ka[kt][2], ka[kt][3], bq[nt][2 * kt], bq[nt][2 * kt + 1]);
+                    mma16816(s1, ka[kt + 1][0], ka[kt + 1][1], ka[kt + 1][2], ka[kt + 1][3], bq[nt][2 * kt + 2],
+                             bq[nt][2 * kt + 3]);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; k++) sc[mtt][nt][k] = s0[k] + s1[k];
             }
         }
-        // page-granular online softmax; lane holds tokens mtt*16 + g (+8), heads nt*8 + 2tid + {0,1}
-        float vsv[MTT][2], vbv[MTT][2];
-#pragma unroll
-        for (int mtt = 0; mtt < MTT; mtt++)
-#pragma unroll
-            for (int r = 0; r < 2; r++) {
-                vsv[mtt][r] = h_load(rec + F::OFF_VS, mtt * 16 + g + 8 * r);
-                vbv[mtt][r] = h_load(rec + F::OFF_VB, mtt * 16 + g + 8 * r);
-            }
-        uint32_t pb[MTT][NT][2];                                          // P'^T B fragments per 16-token tile
+        // online softmax with a lazily moved max; lane holds tokens mtt*16 + g (+8), heads nt*8 + 2tid + {0,1}
+        bool bump = false;
+        float lmx[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            float mx[2] = {-INFINITY, -INFINITY};
+            lmx[nt][0] = lmx[nt][1] = -INFINITY;
 #pragma unroll
             for (int mtt = 0; mtt < MTT; mtt++) {
-                mx[0] = fmaxf(mx[0], fmaxf(sc[mtt][nt][0], sc[mtt][nt][2]));
-                mx[1] = fmaxf(mx[1], fmaxf(sc[mtt][nt][1], sc[mtt][nt][3]));
+                lmx[nt][0] = fmaxf(lmx[nt][0], fmaxf(sc[mtt][nt][0], sc[mtt][nt][2]));
+                lmx[nt][1] = fmaxf(lmx[nt][1], fmaxf(sc[mtt][nt][1], sc[mtt][nt][3]));
             }
-            float corr[2];
+            bump |= lmx[nt][0] > m[nt][0] + TAU || lmx[nt][1] > m[nt][1] + TAU;
+        }
+        if (__any_sync(0xffffffffu, bump)) {                             // rare: move the max to the exact one
 #pragma unroll
-            for (int e = 0; e < 2; e++) {
+            for (int nt = 0; nt < NT; nt++) {
+                float corr[2];
 #pragma unroll
-                for (int off = 4; off < 32; off <<= 1) mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], off));
-                const float mn = fmaxf(m[nt][e], mx[e]);
-                corr[e] = fast_exp2(m[nt][e] - mn);
-                m[nt][e] = mn;
-                l[nt][e] *= corr[e];
-                vbacc[nt][e] *= corr[e];
-            }
+                for (int e = 0; e < 2; e++) {
+                    float mx = lmx[nt][e];
 #pragma unroll
-            for (int mtt = 0; mtt < MTT; mtt++) {
-                float pv[4];
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int e = k & 1, r = k >> 1;
-                    const float p = fast_exp2(sc[mtt][nt][k] - m[nt][e]);
-                    l[nt][e] += p;
-                    vbacc[nt][e] += p * vbv[mtt][r];
-                    pv[k] = p * vsv[mtt][r];
+                    for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                    const float mn = fmaxf(m[nt][e], mx);
+                    corr[e] = fast_exp2(m[nt][e] - mn);
+                    m[nt][e] = mn;
+                    l[nt][e] *= corr[e];
+                    vbacc[nt][e] *= corr[e];
                 }
-                pb[mtt][nt][0] = movmatrix_t(pack_h2(pv[0], pv[1]));       // tokens 0-7 of the tile
-                pb[mtt][nt][1] = movmatrix_t(pack_h2(pv[2], pv[3]));       // tokens 8-15
-            }
-            if (corr[0] != 1.0f || corr[1] != 1.0f) {
 #pragma unroll
                 for (int mt = 0; mt < MT; mt++) {
                     o[mt][nt][0] *= corr[0];
@@ -413,16 +447,38 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
                 }
             }
         }
-        // PV
+        float vsv[MTT][2], vbv[MTT][2];
+#pragma unroll
+        for (int mtt = 0; mtt < MTT; mtt++)
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                vsv[mtt][r] = h_load(rec + F::OFF_VS, mtt * 16 + g + 8 * r);
+                vbv[mtt][r] = h_load(rec + F::OFF_VB, mtt * 16 + g + 8 * r);
+            }
 #pragma unroll
         for (int mtt = 0; mtt < MTT; mtt++) {
+            uint32_t pb[NT][2];                                           // P'^T B fragments of this tile
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                float pv[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int e = k & 1, r = k >> 1;
+                    const float p = fast_exp2(sc[mtt][nt][k] - m[nt][e]);
+                    l[nt][e] += p;
+                    vbacc[nt][e] = fmaf(p, vbv[mtt][r], vbacc[nt][e]);
+                    pv[k] = p * vsv[mtt][r];
+                }
+                pb[nt][0] = movmatrix_t(pack_h2(pv[0], pv[1]));          // tokens 0-7 of the tile
+                pb[nt][1] = movmatrix_t(pack_h2(pv[2], pv[3]));          // tokens 8-15
+            }
             uint32_t va[MT][4];
             v_frags<D, BITS>(rec + F::OFF_VQ + mtt * 16 * F::DC, g, tid, va);
 #pragma unroll
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++)
-                    mma16816(o[mt][nt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb[mtt][nt][0], pb[mtt][nt][1]);
+                    mma16816(o[mt][nt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb[nt][0], pb[nt][1]);
         }
         __syncwarp();
         // refill this slot with page i + NS
@@ -438,7 +494,8 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
     if (!ok) {
         // a copy never completed: record it, wait (bounded) for this warp's copies still in flight, produce NaN
         if (lane == 0) atomicExch(&g_decode_error, 1);
-        for (int i = fail_at + 1; i < fail_at + NS && i < npw; i++) mbar_wait(&wbar[i % NS], uint32_t(i / NS) & 1u);
+        for (int i = fail_at + 1; i < fail_at + NS && i < npw; i++)
+            mbar_wait_u32(bar_u + 8 * (uint32_t(i) % NS), (uint32_t(i) / NS) & 1u);
     }
     ok = __syncthreads_and(ok);
 
@@ -473,16 +530,28 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
                 }
             }
         }
-    // the tail page: exact K from tail_k, V rows from its record; warp 0, fp32 on the CUDA cores
-    if (wid == 0) {
+    // the tail page: exact K from tail_k, V rows from its record, fp32 on the CUDA cores; warp w takes heads w, w+NW..
+    {
         const bool has_tail = tail_n > 0 && z == n_splits - 1;
-        for (int hd = 0; hd < G; hd++) {
+        const IN* tk = has_tail ? tail_k + ((int64_t(tail_idx[s]) * H + h) * P + min(lane, P - 1)) * D : nullptr;
+        const uint8_t* trec = has_tail ? hcache + int64_t(bt[full]) * block_stride : nullptr;
+        constexpr int R = D / WARP;
+        for (int hd = wid; hd < G; hd += NW) {
+            const float* qh = qsm + hd * D;
+            float qkref = 0.0f;                                          // q . kb_ref (the shift of every score)
+            for (int d = lane; d < D; d += WARP) qkref = fmaf(qh[d], kbr[d], qkref);
+            qkref = warp_sum(qkref);
             float x = -INFINITY;
             if (has_tail && lane < tail_n) {
-                const IN* tk = tail_k + ((int64_t(tail_idx[s]) * H + h) * P + lane) * D;
+                constexpr int VE = 16 / sizeof(IN);                      // elements per 16-byte load
                 float acc = 0.0f;
-                for (int d = 0; d < D; d++) acc += qsm[hd * D + d] * (to_f32(tk[d]) - kbr[d]);
-                x = acc;
+                for (int d0 = 0; d0 < D; d0 += VE) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(tk + d0);
+                    const IN* e = reinterpret_cast<const IN*>(&raw);
+#pragma unroll
+                    for (int k = 0; k < VE; k++) acc = fmaf(qh[d0 + k], to_f32(e[k]), acc);
+                }
+                x = acc - qkref;
             }
             const float mx = warp_max(x);
             const float p = (has_tail && lane < tail_n) ? fast_exp2(x - mx) : 0.0f;
@@ -491,16 +560,18 @@ __global__ void __launch_bounds__(MMA_NW * WARP) decode_mma_kernel(
                 c_m[NW * G + hd] = has_tail ? mx : -INFINITY;
                 c_l[NW * G + hd] = lsum;
             }
-            const uint8_t* trec = has_tail ? hcache + int64_t(bt[full]) * block_stride : nullptr;
-            for (int d = lane; d < D; d += WARP) {
-                float acc = 0.0f;
-                for (int t = 0; t < tail_n && has_tail; t++) {
-                    const float pt = __shfl_sync(0xffffffffu, p, t);
-                    const float c = float(code_at<D, BITS>(trec + F::OFF_VQ + t * F::DC, d));
-                    acc += pt * (c * h_load(trec + F::OFF_VS, t) + h_load(trec + F::OFF_VB, t));
-                }
-                c_acc[(NW * G + hd) * D + d] = acc;
+            float acc[R];
+#pragma unroll
+            for (int i = 0; i < R; i++) acc[i] = 0.0f;
+            for (int t = 0; t < tail_n && has_tail; t++) {               // lane holds dims lane + 32 i
+                const float pt = __shfl_sync(0xffffffffu, p, t);
+                const float vs = h_load(trec + F::OFF_VS, t) * pt, vb = h_load(trec + F::OFF_VB, t) * pt;
+#pragma unroll
+                for (int i = 0; i < R; i++)
+                    acc[i] = fmaf(float(code_at<D, BITS>(trec + F::OFF_VQ + t * F::DC, lane + WARP * i)), vs, acc[i] + vb);
             }
+#pragma unroll
+            for (int i = 0; i < R; i++) c_acc[(NW * G + hd) * D + lane + WARP * i] = acc[i];
         }
     }
     __syncthreads();
@@ -538,26 +609,22 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
                const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
                int32_t n_seqs, cudaStream_t stream) {
-    using C = MmaCfg<D, BITS, P>;
-    const size_t merge = sizeof(float) * (size_t(MMA_NW + 1) * G * D + 2 * size_t(MMA_NW + 1) * G);
-    const size_t ring = C::RING > merge ? size_t(C::RING) : (merge + 127) / 128 * 128;
-    const size_t smem = ring + sizeof(uint64_t) * MMA_NW * C::NS + sizeof(float) * (size_t(G) * D + D);
+    using C = MmaCfg<D, BITS, P, NT>;
     auto kern = decode_mma_kernel<D, BITS, P, NT, IN>;
-    if (ring != size_t(C::RING)) return set_error(KUSH_ERR_UNSUPPORTED, "decode: group %d too large for the ring", G);
     static unsigned long long attr_set = 0;             // one bit per device: the attribute is per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_set >> (dev & 63) & 1ull)) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "decode: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         attr_set |= 1ull << (dev & 63);
     }
     dim3 grid(n_seqs, hkv, n_splits);
-    kern<<<grid, MMA_NW * WARP, smem, stream>>>(static_cast<const IN*>(q), static_cast<IN*>(out),
-                                                static_cast<const uint8_t*>(cache), block_stride, head_stride,
-                                                static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens,
-                                                max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml,
-                                                part_o);
+    kern<<<grid, MMA_NW * WARP, C::SMEM, stream>>>(static_cast<const IN*>(q), static_cast<IN*>(out),
+                                                   static_cast<const uint8_t*>(cache), block_stride, head_stride,
+                                                   static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens,
+                                                   max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml,
+                                                   part_o);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
