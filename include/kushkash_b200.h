@@ -81,6 +81,23 @@ int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
                       int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o, int32_t n_seqs,
                       void *stream);
 
+/* Size of the fixed split-KV scratch used by kush_sm100_decode_noalloc: 2M floats (8 MiB) per GPU. */
+#define KUSH_NOALLOC_SCRATCH_FLOATS (1 << 21)
+
+/* kush_sm100_decode followed, when n_splits > 1, by kush_sm100_combine, for callers that cannot allocate or pass a
+ * scratch buffer (a serving engine's decode step that must not allocate, or a C FFI caller without a CUDA
+ * allocator): the split partials live in a fixed 8 MiB device array inside the library, which every GPU that loads
+ * the library holds until exit.  No counterpart in the reference (its decode takes a caller-allocated `work`).
+ * Limit: n_seqs * hkv * n_splits * group * (head_dim + 2) <= KUSH_NOALLOC_SCRATCH_FLOATS, else KUSH_ERR_ARG.
+ * The first call on each device looks up the array's device address (make it before any stream capture); all
+ * calls share the array, so calls that overlap on the GPU race and must be serialised by the caller.  Allocates
+ * nothing. */
+int kush_sm100_decode_noalloc(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+                              const void *q, void *out, const void *cache, int64_t block_stride, int64_t head_stride,
+                              const void *tail_k, const int32_t *tail_idx, const int32_t *block_table,
+                              const int32_t *seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
+                              int32_t n_seqs, void *stream);
+
 /* Split-KV merge.  Replaces kush_combine (kushkash/kush/gpu.mojo:469-491) as launched by Ops.decode
  * (kushkash/_ops.py:212-213): out = sum_z exp(M_z - M) O_z / sum_z exp(M_z - M) L_z per (s, h, g). */
 int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void *out, const float *part_ml,

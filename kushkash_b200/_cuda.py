@@ -33,6 +33,8 @@ SIGNATURES = {
     "kush_sm100_decode": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32, _i32,
                           _p, _p, _i32, _p],
     "kush_sm100_combine": [_i32, _i32, _i32, _p, _p, _p, _i32, _i32, _i32, _p],
+    "kush_sm100_decode_noalloc": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,
+                                  _f32, _i32, _i32, _p],
     "kush_sm100_decode_tensor_cores": [_i32, _i32, _i32, _i32, _i32],
     "kush_sm100_fwht": [_i32, _i32, _p, _p, _i64, _i64, _i64, _p],
     "kush_sm100_unpack": [_i32, _i32, _i32, _i32, _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _i64,
