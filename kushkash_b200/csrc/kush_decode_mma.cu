@@ -130,10 +130,10 @@ struct Lay {
             return tid * CB + 4 * (e >> 1) + 2 * (e & 1);
         }
     }
-    // output dim of PV fragment row r (0..15) in m-tile mt for lane group g (rows g and g + 8 of the tile)
+    // output dim of PV fragment row g (hi = 0) or g + 8 (hi = 1) of m-tile mt (the v_frags layout)
     __device__ static int vdim(int g, int mt, int hi) {
-        if constexpr (BITS == 4) return g * VB + mt + hi * (D / 2);
-        else return g * VB + mt + hi * MT;
+        if constexpr (BITS == 4) return hi * (D / 2) + 16 * (mt >> 1) + 2 * g + (mt & 1);
+        else return 16 * mt + 2 * g + hi;
     }
 };
 
@@ -220,51 +220,48 @@ __device__ __forceinline__ void k_frags(const uint8_t* row0, const uint8_t* row1
     }
 }
 
-// V^T A fragments of one 16-token tile: lane group g reads VB bytes of token rows 2tid, 2tid+1, 2tid+8, 2tid+9;
-// a[mt][0..3] = (row g | row g+8) x (tokens 2tid,2tid+1 | 2tid+8,2tid+9), exact codes
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// V^T A fragments of one 16-token tile from the record's V rows at shared address vq.  The rows are read as 8x8
+// matrices of 16-bit units (8 tokens x 16 bytes) with ldmatrix.trans, which hands lane (g, tid) the 2 bytes 2g, 2g+1
+// of a 16-byte chunk for tokens 2tid and 2tid+1 in one register: the token interleave the A fragment needs.
+//   int4: chunk k, byte b gives m-tile 2k + b: row g = low nibbles (dim 16k + 2g + b), row g+8 = high nibbles
+//   int8: chunk k gives m-tile k: row g = byte 2g (dim 16k + 2g), row g+8 = byte 2g+1
+// a[mt] = {row g x tokens 2tid,2tid+1 | row g+8 x same | row g x tokens 2tid+8,+9 | row g+8 x same}, exact codes.
 template <int D, int BITS>
-__device__ __forceinline__ void v_frags(const uint8_t* vq, int g, int tid, uint32_t (&a)[D / 16][4]) {
+__device__ __forceinline__ void v_frags(uint32_t vq, int lane, uint32_t (&a)[D / 16][4]) {
     using L = Lay<D, BITS>;
-    constexpr int NWV = (L::VB + 3) / 4;        // 32-bit words per lane per row
-    uint32_t w[4][NWV];
+    constexpr int NCH = L::DC / 16;                       // 16-byte chunks per token row
+    const int mi = lane >> 3, rr = lane & 7;               // this lane addresses row rr of matrix mi of each load
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const uint8_t* p = vq + (2 * tid + (r & 1) + 8 * (r >> 1)) * L::DC + g * L::VB;
-        if constexpr (L::VB == 4) {
-            w[r][0] = *reinterpret_cast<const uint32_t*>(p);
-        } else if constexpr (L::VB == 8) {
-            const uint2 v = *reinterpret_cast<const uint2*>(p);
-            w[r][0] = v.x;
-            w[r][1] = v.y;
-        } else {
+    for (int ld = 0; ld < NCH / 2; ld++) {
+        // matrices of load ld: (tokens 0-7, chunk 2ld), (0-7, 2ld+1), (8-15, 2ld), (8-15, 2ld+1)
+        uint32_t r[4];
+        ldsm_x4_trans(vq + ((mi >> 1) * 8 + rr) * L::DC + 16 * (2 * ld + (mi & 1)), r);
 #pragma unroll
-            for (int i = 0; i < NWV / 4; i++) {
-                const uint4 v = reinterpret_cast<const uint4*>(p)[i];
-                w[r][4 * i] = v.x;
-                w[r][4 * i + 1] = v.y;
-                w[r][4 * i + 2] = v.z;
-                w[r][4 * i + 3] = v.w;
-            }
-        }
-    }
-#pragma unroll
-    for (int mt = 0; mt < L::MT; mt++) {
-#pragma unroll
-        for (int pr = 0; pr < 2; pr++) {                       // token pair (2tid, 2tid+1) or (2tid+8, 2tid+9)
+        for (int c = 0; c < 2; c++) {                     // chunk k = 2 ld + c
+            const int k = 2 * ld + c;
+            const uint32_t lo_t = r[c], hi_t = r[2 + c];  // tokens 2tid,2tid+1 | 2tid+8,2tid+9
             if constexpr (BITS == 4) {
-                const int j = mt, wi = j >> 2, jj = j & 3;
-                const uint32_t sel = jj | (jj << 4) | ((4 + jj) << 8) | ((4 + jj) << 12);
-                const uint32_t x = prmt(w[2 * pr][wi], w[2 * pr + 1][wi], sel);     // halves: byte j of t0, t1
-                a[mt][2 * pr] = h2_sub(and_xor(x, 0x000F000Fu, H2_1032), H2_1032);                 // row g
-                a[mt][2 * pr + 1] = h2_fma(and_xor(x, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);  // row g+8
-            } else {
 #pragma unroll
-                for (int hi = 0; hi < 2; hi++) {
-                    const int j = mt + hi * L::MT, wi = j >> 2, jj = j & 3;
-                    const uint32_t sel = jj | (jj << 4) | ((4 + jj) << 8) | ((4 + jj) << 12);
-                    const uint32_t x = prmt(w[2 * pr][wi], w[2 * pr + 1][wi], sel);
-                    a[mt][2 * pr + hi] = h2_sub(and_xor(x, 0x00FF00FFu, 0x64806480u), H2_1152);
+                for (int b = 0; b < 2; b++) {
+                    const uint32_t x0 = b ? lo_t >> 8 : lo_t, x1 = b ? hi_t >> 8 : hi_t;
+                    const int mt = 2 * k + b;
+                    a[mt][0] = h2_sub(and_xor(x0, 0x000F000Fu, H2_1032), H2_1032);
+                    a[mt][1] = h2_fma(and_xor(x0, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);
+                    a[mt][2] = h2_sub(and_xor(x1, 0x000F000Fu, H2_1032), H2_1032);
+                    a[mt][3] = h2_fma(and_xor(x1, 0x00F000F0u, 0x64806480u), H2_INV16, H2_M72);
                 }
+            } else {
+                const uint32_t u0 = lo_t ^ 0x80808080u, u1 = hi_t ^ 0x80808080u;   // signed code -> c + 128
+                a[k][0] = h2_sub(prmt(u0, 0x64646464u, 0x4240), H2_1152);       // byte 2g of tokens t0, t1
+                a[k][1] = h2_sub(prmt(u0, 0x64646464u, 0x4341), H2_1152);       // byte 2g + 1
+                a[k][2] = h2_sub(prmt(u1, 0x64646464u, 0x4240), H2_1152);
+                a[k][3] = h2_sub(prmt(u1, 0x64646464u, 0x4341), H2_1152);
             }
         }
     }
@@ -406,8 +403,12 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
                     mma16816(s1, ka[kt + 1][0], ka[kt + 1][1], ka[kt + 1][2], ka[kt + 1][3], bq[nt][2 * kt + 2],
                              bq[nt][2 * kt + 3]);
                 }
-#pragma unroll
-                for (int k = 0; k < 4; k++) sc[mtt][nt][k] = s0[k] + s1[k];
+                const float2 a01 = __fadd2_rn(make_float2(s0[0], s0[1]), make_float2(s1[0], s1[1]));
+                const float2 a23 = __fadd2_rn(make_float2(s0[2], s0[3]), make_float2(s1[2], s1[3]));
+                sc[mtt][nt][0] = a01.x;
+                sc[mtt][nt][1] = a01.y;
+                sc[mtt][nt][2] = a23.x;
+                sc[mtt][nt][3] = a23.y;
             }
         }
         // online softmax with a lazily moved max; lane holds tokens mtt*16 + g (+8), heads nt*8 + 2tid + {0,1}
@@ -460,20 +461,25 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             uint32_t pb[NT][2];                                           // P'^T B fragments of this tile
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                float pv[4];
+                // head pair (2tid, 2tid+1) of token row r in packed fp32x2 arithmetic (sm_100 FADD2/FFMA2/FMUL2)
+                const float2 negm = make_float2(-m[nt][0], -m[nt][1]);
+                float2 lp = make_float2(l[nt][0], l[nt][1]), vp = make_float2(vbacc[nt][0], vbacc[nt][1]);
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int e = k & 1, r = k >> 1;
-                    const float p = fast_exp2(sc[mtt][nt][k] - m[nt][e]);
-                    l[nt][e] += p;
-                    vbacc[nt][e] = fmaf(p, vbv[mtt][r], vbacc[nt][e]);
-                    pv[k] = p * vsv[mtt][r];
+                for (int r = 0; r < 2; r++) {
+                    const float2 d = __fadd2_rn(make_float2(sc[mtt][nt][2 * r], sc[mtt][nt][2 * r + 1]), negm);
+                    const float2 p = make_float2(fast_exp2(d.x), fast_exp2(d.y));
+                    lp = __fadd2_rn(lp, p);
+                    vp = __ffma2_rn(p, make_float2(vbv[mtt][r], vbv[mtt][r]), vp);
+                    const float2 pv = __fmul2_rn(p, make_float2(vsv[mtt][r], vsv[mtt][r]));
+                    pb[nt][r] = movmatrix_t(pack_h2(pv.x, pv.y));        // r = 0: tokens 0-7, 1: tokens 8-15
                 }
-                pb[nt][0] = movmatrix_t(pack_h2(pv[0], pv[1]));          // tokens 0-7 of the tile
-                pb[nt][1] = movmatrix_t(pack_h2(pv[2], pv[3]));          // tokens 8-15
+                l[nt][0] = lp.x;
+                l[nt][1] = lp.y;
+                vbacc[nt][0] = vp.x;
+                vbacc[nt][1] = vp.y;
             }
             uint32_t va[MT][4];
-            v_frags<D, BITS>(rec + F::OFF_VQ + mtt * 16 * F::DC, g, tid, va);
+            v_frags<D, BITS>(smem_u32(rec) + F::OFF_VQ + mtt * 16 * F::DC, lane, va);
 #pragma unroll
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
