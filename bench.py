@@ -43,12 +43,13 @@ FALLBACK_HBM_GBS = 6650.0
 
 # ---------------------------------------------------------------- workload
 class Geometry:
-    def __init__(self, a):
+    def __init__(self, a, hkv: int = 8):
         self.L, self.B, self.N, self.P = a.layers, a.batch, a.context, a.page
-        self.HQ, self.HKV, self.D, self.bits = 32, 8, 128, 4
+        self.HQ, self.HKV, self.D, self.bits = 4 * hkv, hkv, 128, 4
         self.G = self.HQ // self.HKV
         self.DC = self.D // 2 if self.bits == 4 else self.D
         self.RB = 2 * self.P * self.DC + 4 * self.D + 4 * self.P
+        self.long = getattr(a, "workload", "batch") == "long"
 
     def packed_bytes(self, n: int, seqs: int | None = None) -> int:
         """Packed-KV bytes one decode reads for `seqs` sequences of n tokens: full pages' records plus the partial
@@ -62,6 +63,14 @@ class Geometry:
         return self.packed_bytes(n) + self.B * self.HQ * self.D * 2 * 2
 
     def describe(self) -> dict:
+        if self.long:
+            return {"workload": f"BASELINE config 4: Qwen3-8B attention geometry, {self.L} layers, int4, batch {self.B} x "
+                                f"{self.N} context, page {self.P}; kv heads partitioned over the GPUs, one step = append "
+                                "+ split-KV decode + output all_gather per layer",
+                    "model": "Qwen3-8B (attention geometry only: 32 q heads, 8 kv heads, head_dim 128)",
+                    "seq_len": self.N, "global_batch": self.B, "layers": self.L, "page": self.P, "bits": self.bits,
+                    "kv_heads_per_gpu": self.HKV, "head_dim": self.D,
+                    "l2": "inputs larger than L2 (records of all layers per step, no flush needed)"}
         return {"workload": f"BASELINE config 3: Llama-3.1-8B attention geometry, {self.L} layers, int4, "
                             f"batch {self.B} x {self.N} context, page {self.P}; one step = append + decode per layer",
                 "model": "Llama-3.1-8B (attention geometry only: 32 q heads, 8 kv heads, head_dim 128)",
@@ -320,7 +329,13 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["batch", "long"], default="batch",
+                    help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned)")
     a = ap.parse_args()
+    if a.workload == "long":
+        for k, v in (("batch", 4), ("context", 131072), ("page", 32), ("layers", 8)):
+            if getattr(a, k) == ap.get_default(k):
+                setattr(a, k, v)
     if a.warmup < 3 and a.impl == "ours":
         print("bench.py: --warmup < 3 is raised to 3 (timing rule)", file=sys.stderr)
         a.warmup = 3
@@ -331,6 +346,9 @@ def main() -> None:
 
     if a.impl == "reference":
         run_reference(a, geo, world, rank)
+        return
+    if a.workload == "long":
+        run_long(a, world, rank, local)
         return
 
     torch.cuda.set_device(local)
@@ -452,6 +470,82 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     del graph, dgraph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_long(a, world: int, rank: int, local: int) -> None:
+    """4 sequences of 131072 tokens; rank r owns kv heads [8r/N, 8(r+1)/N) of every sequence and
+    layer, runs append + split-KV decode for them, and the per-layer [4, 32/N, 128] outputs are all_gathered over NCCL
+    (the only collective).  Strong scaling: the total work is fixed as N grows."""
+    from kushkash_b200.shard import gather_heads, kv_head_range
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    h0, h1 = kv_head_range(8, rank, world)
+    geo = Geometry(a, hkv=h1 - h0)
+    full = Geometry(a, hkv=8)
+    eng = Engine(geo, dev, seed=4321 + rank, extra_tokens=a.warmup + a.steps + 8)
+    outs = [torch.empty(geo.B, full.HQ, geo.D, dtype=torch.bfloat16, device=dev) for _ in range(geo.L)]
+
+    def step():
+        for layer in range(geo.L):
+            eng.ops.append(eng.k_new[layer], eng.v_new[layer], eng.seq_lens[layer], eng.tail_idx, eng.pool[layer],
+                           eng.block_table, eng.tail_k[layer], pos_offset=0, advance=True)
+            eng.ops.decode(eng.q[layer], eng.out[layer], eng.pool[layer], eng.block_table, eng.seq_lens[layer],
+                           eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work)
+            outs[layer].copy_(gather_heads(eng.out[layer]) if dist is not None else eng.out[layer])
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(a.warmup - 1):
+        step()
+    graph = None
+    if dist is None:                            # one GPU: the whole step as one CUDA graph
+        graph = capture(step, dev)
+        run = graph.replay
+    else:                                       # collectives are not captured: eager steps, NCCL gathers in between
+        run = step
+        step()
+    n0 = int(eng.seq_lens[0, 0].item())
+    barrier()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    byts = sum(full.packed_bytes(n0 + i + 1) for i in range(a.steps)) * geo.L
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        ms_step = ms / a.steps
+        value = byts / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
+            "data": "synthetic (seeded bf16 N(0,1) K/V/q with per-channel key offsets N(0, 2), BASELINE config 4 shapes)",
+            "config": {**full.describe(), "parallelism": f"kv heads partitioned over {world} GPU(s), all_gather of "
+                       "outputs per layer", "n_splits": eng.ns},
+            "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
+            "us_per_layer_step": round(ms_step * 1e3 / geo.L, 2),
+            "decode_tokens_per_s": round(geo.B / (ms_step / 1e3), 1), "clocks": clocks,
+            "gpu_launches": a.steps * eng.launches_per_step(), "cuda_graph": graph is not None}), flush=True)
+    del graph, eng
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

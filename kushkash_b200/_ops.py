@@ -38,13 +38,16 @@ def _byte_strides(cache: torch.Tensor) -> tuple[int, int]:
     return cache.stride(0) * e, cache.stride(1) * e
 
 
-def split_factor(num_seqs: int, num_kv_heads: int, max_full_pages: int, sms: int) -> int:
-    """Split-KV factor: a power of two, grown while the grid has fewer than ~8 blocks per SM and every split keeps
-    >= 4 pages; at most MAX_SPLITS (the reference: ~6 blocks per SM, <= 32, kushkash/_ops.py:182-189)."""
-    ns = 1
-    while ns < MAX_SPLITS and num_seqs * num_kv_heads * ns < 8 * sms and max_full_pages // (2 * ns) >= 4:
-        ns *= 2
-    return ns
+def split_factor(num_seqs: int, num_kv_heads: int, max_full_pages: int, sms: int, ctas_per_sm: int = 4) -> int:
+    """Split-KV factor: enough splits that the decode grid fills the ~ctas_per_sm resident CTAs of every SM once (any
+    integer, not only powers of two), at most MAX_SPLITS and at least 4 pages per split; 1 when the (sequence, kv
+    head) units alone fill half the GPU.  (The reference grows powers of two up to 32 while the grid has fewer than
+    6 blocks per SM, kushkash/_ops.py:182-189; on B200 fewer, fuller splits measured faster: per-split setup, merge
+    and the combine grow with the split count.)"""
+    units, cap = num_seqs * num_kv_heads, ctas_per_sm * sms
+    if units == 0 or units * 2 >= cap or max_full_pages < 8:
+        return 1
+    return max(1, min(MAX_SPLITS, cap // units, max_full_pages // 4))
 
 
 class Ops:

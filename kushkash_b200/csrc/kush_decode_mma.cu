@@ -279,7 +279,8 @@ struct MmaCfg {
     // shared memory: [bars | ring (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D])]
     static constexpr int SMEM = BARS + RING + 4 * (GMAX * D + D);
     // CTAs per SM the register budget targets (the larger tiles need more registers per thread)
-    static constexpr int MINB = (D == 64 || (D == 128 && P == 16 && NT == 1)) ? 4 : NT == 1 && D == 128 ? 3 : 2;
+    static constexpr int MINB = (D == 64 || (D == 128 && NT == 1 && !(BITS == 8 && P == 32))) ? 4
+                                : NT == 1 && D == 128 ? 3 : 2;
 };
 
 // scores more than 2^TAU above the running max trigger a rescale; below that the stale max is kept (weights
@@ -382,82 +383,78 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             break;
         }
         const uint8_t* rec = wring + slot * C::RB;
-        // per-page K scale and bias pairs for this lane's dims (K' = c * ks + (kb - kb_ref))
-        uint32_t ks[2 * KT], dkb[2 * KT];
-        load_pairs<D, BITS>(rec + F::OFF_KS, tid, ks);
-        load_pairs<D, BITS>(rec + F::OFF_KB, tid, dkb);
-#pragma unroll
-        for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref[e]);
-        float sc[MTT][NT][4];
+        // one 16-token tile at a time (P = 32 pages have two): QK, online softmax, PV.  The softmax is tile-granular,
+        // which keeps the register footprint of both page sizes the same.
 #pragma unroll
         for (int mtt = 0; mtt < MTT; mtt++) {
-            uint32_t ka[KT][4];                                           // A fragments of this 16-token tile
-            const uint8_t* r0 = rec + (mtt * 16 + g) * F::DC + tid * L::CB;
-            k_frags<D, BITS>(r0, r0 + 8 * F::DC, ks, dkb, ka);
+            float sc[NT][4];
+            {
+                // the page's K scale and bias pairs for this lane's dims (K' = c * ks + (kb - kb_ref)); reloaded per
+                // tile rather than held across the tiles of a 32-token page (register pressure)
+                uint32_t ks[2 * KT], dkb[2 * KT];
+                load_pairs<D, BITS>(rec + F::OFF_KS, tid, ks);
+                load_pairs<D, BITS>(rec + F::OFF_KB, tid, dkb);
+#pragma unroll
+                for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref[e]);
+                uint32_t ka[KT][4];                                       // A fragments of this 16-token tile
+                const uint8_t* r0 = rec + (mtt * 16 + g) * F::DC + tid * L::CB;
+                k_frags<D, BITS>(r0, r0 + 8 * F::DC, ks, dkb, ka);
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // two chains
+#pragma unroll
+                    for (int kt = 0; kt < KT; kt += 2) {
+                        mma16816(s0, ka[kt][0], ka[kt][1], ka[kt][2], ka[kt][3], bq[nt][2 * kt], bq[nt][2 * kt + 1]);
+                        mma16816(s1, ka[kt + 1][0], ka[kt + 1][1], ka[kt + 1][2], ka[kt + 1][3], bq[nt][2 * kt + 2],
+                                 bq[nt][2 * kt + 3]);
+                    }
+                    const float2 a01 = __fadd2_rn(make_float2(s0[0], s0[1]), make_float2(s1[0], s1[1]));
+                    const float2 a23 = __fadd2_rn(make_float2(s0[2], s0[3]), make_float2(s1[2], s1[3]));
+                    sc[nt][0] = a01.x;
+                    sc[nt][1] = a01.y;
+                    sc[nt][2] = a23.x;
+                    sc[nt][3] = a23.y;
+                }
+            }
+            // online softmax with a lazily moved max; lane holds tokens mtt*16 + g (+8), heads nt*8 + 2tid + {0,1}
+            bool bump = false;
+            float lmx[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // two chains
-#pragma unroll
-                for (int kt = 0; kt < KT; kt += 2) {
-                    mma16816(s0, ka[kt][0], ka[kt][1], ka[kt][2], ka[kt][3], bq[nt][2 * kt], bq[nt][2 * kt + 1]);
-                    mma16816(s1, ka[kt + 1][0], ka[kt + 1][1], ka[kt + 1][2], ka[kt + 1][3], bq[nt][2 * kt + 2],
-                             bq[nt][2 * kt + 3]);
-                }
-                const float2 a01 = __fadd2_rn(make_float2(s0[0], s0[1]), make_float2(s1[0], s1[1]));
-                const float2 a23 = __fadd2_rn(make_float2(s0[2], s0[3]), make_float2(s1[2], s1[3]));
-                sc[mtt][nt][0] = a01.x;
-                sc[mtt][nt][1] = a01.y;
-                sc[mtt][nt][2] = a23.x;
-                sc[mtt][nt][3] = a23.y;
+                lmx[nt][0] = fmaxf(sc[nt][0], sc[nt][2]);
+                lmx[nt][1] = fmaxf(sc[nt][1], sc[nt][3]);
+                bump |= lmx[nt][0] > m[nt][0] + TAU || lmx[nt][1] > m[nt][1] + TAU;
             }
-        }
-        // online softmax with a lazily moved max; lane holds tokens mtt*16 + g (+8), heads nt*8 + 2tid + {0,1}
-        bool bump = false;
-        float lmx[NT][2];
+            if (__any_sync(0xffffffffu, bump)) {                         // rare: move the max to the exact one
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            lmx[nt][0] = lmx[nt][1] = -INFINITY;
+                for (int nt = 0; nt < NT; nt++) {
+                    float corr[2];
 #pragma unroll
-            for (int mtt = 0; mtt < MTT; mtt++) {
-                lmx[nt][0] = fmaxf(lmx[nt][0], fmaxf(sc[mtt][nt][0], sc[mtt][nt][2]));
-                lmx[nt][1] = fmaxf(lmx[nt][1], fmaxf(sc[mtt][nt][1], sc[mtt][nt][3]));
-            }
-            bump |= lmx[nt][0] > m[nt][0] + TAU || lmx[nt][1] > m[nt][1] + TAU;
-        }
-        if (__any_sync(0xffffffffu, bump)) {                             // rare: move the max to the exact one
+                    for (int e = 0; e < 2; e++) {
+                        float mx = lmx[nt][e];
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                float corr[2];
+                        for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                        const float mn = fmaxf(m[nt][e], mx);
+                        corr[e] = fast_exp2(m[nt][e] - mn);
+                        m[nt][e] = mn;
+                        l[nt][e] *= corr[e];
+                        vbacc[nt][e] *= corr[e];
+                    }
 #pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    float mx = lmx[nt][e];
-#pragma unroll
-                    for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-                    const float mn = fmaxf(m[nt][e], mx);
-                    corr[e] = fast_exp2(m[nt][e] - mn);
-                    m[nt][e] = mn;
-                    l[nt][e] *= corr[e];
-                    vbacc[nt][e] *= corr[e];
-                }
-#pragma unroll
-                for (int mt = 0; mt < MT; mt++) {
-                    o[mt][nt][0] *= corr[0];
-                    o[mt][nt][1] *= corr[1];
-                    o[mt][nt][2] *= corr[0];
-                    o[mt][nt][3] *= corr[1];
+                    for (int mt = 0; mt < MT; mt++) {
+                        o[mt][nt][0] *= corr[0];
+                        o[mt][nt][1] *= corr[1];
+                        o[mt][nt][2] *= corr[0];
+                        o[mt][nt][3] *= corr[1];
+                    }
                 }
             }
-        }
-        float vsv[MTT][2], vbv[MTT][2];
-#pragma unroll
-        for (int mtt = 0; mtt < MTT; mtt++)
+            float vsv[2], vbv[2];
 #pragma unroll
             for (int r = 0; r < 2; r++) {
-                vsv[mtt][r] = h_load(rec + F::OFF_VS, mtt * 16 + g + 8 * r);
-                vbv[mtt][r] = h_load(rec + F::OFF_VB, mtt * 16 + g + 8 * r);
+                vsv[r] = h_load(rec + F::OFF_VS, mtt * 16 + g + 8 * r);
+                vbv[r] = h_load(rec + F::OFF_VB, mtt * 16 + g + 8 * r);
             }
-#pragma unroll
-        for (int mtt = 0; mtt < MTT; mtt++) {
             uint32_t pb[NT][2];                                           // P'^T B fragments of this tile
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
@@ -466,11 +463,11 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
                 float2 lp = make_float2(l[nt][0], l[nt][1]), vp = make_float2(vbacc[nt][0], vbacc[nt][1]);
 #pragma unroll
                 for (int r = 0; r < 2; r++) {
-                    const float2 d = __fadd2_rn(make_float2(sc[mtt][nt][2 * r], sc[mtt][nt][2 * r + 1]), negm);
+                    const float2 d = __fadd2_rn(make_float2(sc[nt][2 * r], sc[nt][2 * r + 1]), negm);
                     const float2 p = make_float2(fast_exp2(d.x), fast_exp2(d.y));
                     lp = __fadd2_rn(lp, p);
-                    vp = __ffma2_rn(p, make_float2(vbv[mtt][r], vbv[mtt][r]), vp);
-                    const float2 pv = __fmul2_rn(p, make_float2(vsv[mtt][r], vsv[mtt][r]));
+                    vp = __ffma2_rn(p, make_float2(vbv[r], vbv[r]), vp);
+                    const float2 pv = __fmul2_rn(p, make_float2(vsv[r], vsv[r]));
                     pb[nt][r] = movmatrix_t(pack_h2(pv.x, pv.y));        // r = 0: tokens 0-7, 1: tokens 8-15
                 }
                 l[nt][0] = lp.x;

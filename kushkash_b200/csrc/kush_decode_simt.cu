@@ -171,28 +171,27 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     }
 }
 
-// grid (S, Hkv), block 256: merge split-K partials (kushkash/kush/gpu.mojo:469-491 kush_combine)
+// grid (S * Hkv * G), block D: merge the split-K partials of one (sequence, kv head, q head); thread d owns output
+// dim d (kushkash/kush/gpu.mojo:469-491 kush_combine, with one block per q head so long split lists run in parallel)
 template <class IN>
 __global__ void __launch_bounds__(256) combine_kernel(IN* __restrict__ out, const float* __restrict__ part_ml,
-                                                      const float* __restrict__ part_o, int n_splits, int H, int G, int D) {
-    const int s = blockIdx.x, h = blockIdx.y;
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const int g = idx / D, d = idx % D;
-        const int64_t base = (int64_t(s) * H + h) * n_splits;
-        float M = -INFINITY;
-        for (int z = 0; z < n_splits; z++) M = fmaxf(M, part_ml[((base + z) * G + g) * 2]);
-        float L = 0.0f, o = 0.0f;
-        for (int z = 0; z < n_splits; z++) {
-            const int64_t pb = (base + z) * G + g;
-            const float mz = part_ml[pb * 2];
-            if (mz > -INFINITY) {
-                const float f = __expf(mz - M);
-                L += part_ml[pb * 2 + 1] * f;
-                o += f * part_o[pb * D + d];
-            }
+                                                      const float* __restrict__ part_o, int n_splits, int G, int D) {
+    const int64_t sh = blockIdx.x / G, g = blockIdx.x % G;
+    const int d = threadIdx.x;
+    const float* ml = part_ml + (sh * n_splits * G + g) * 2;     // split z at ml[2 z G]
+    const float* po = part_o + (sh * n_splits * G + g) * D + d;  // split z at po[z G D]
+    float M = -INFINITY;
+    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ml[2 * int64_t(z) * G]);
+    float L = 0.0f, o = 0.0f;
+    for (int z = 0; z < n_splits; z++) {
+        const float mz = ml[2 * int64_t(z) * G];
+        if (mz > -INFINITY) {
+            const float f = __expf(mz - M);
+            L = fmaf(ml[2 * int64_t(z) * G + 1], f, L);
+            o = fmaf(f, po[int64_t(z) * G * D], o);
         }
-        out[(int64_t(s) * H + h) * G * D + idx] = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
     }
+    out[(sh * G + g) * D + d] = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
 }
 
 template <int D, int BITS, int P, class IN>
@@ -216,8 +215,9 @@ int launch_decode_simt(const void* q, void* out, const void* cache, int64_t bloc
 template <class IN>
 int launch_combine(void* out, const float* part_ml, const float* part_o, int32_t n_splits, int32_t hkv, int32_t G,
                    int32_t D, int32_t n_seqs, cudaStream_t stream) {
-    dim3 grid(n_seqs, hkv);
-    combine_kernel<IN><<<grid, 256, 0, stream>>>(static_cast<IN*>(out), part_ml, part_o, n_splits, hkv, G, D);
+    const int64_t blocks = int64_t(n_seqs) * hkv * G;
+    if (blocks > 0x7fffffff) return set_error(KUSH_ERR_ARG, "kush_sm100_combine: grid too large");
+    combine_kernel<IN><<<unsigned(blocks), D, 0, stream>>>(static_cast<IN*>(out), part_ml, part_o, n_splits, G, D);
     return check_launch("kush_sm100_combine");
 }
 

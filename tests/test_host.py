@@ -68,14 +68,15 @@ def test_ops_refuses_cpu_device():
 
 def test_split_factor():
     from kushkash_b200._ops import split_factor
-    assert split_factor(256, 8, 256, 148) == 1                    # 2048 units already
-    assert split_factor(4, 8, 4096, 148) == 64                    # config 4, one GPU: 64 splits
-    assert split_factor(4, 1, 4096, 148) == 256                   # config 4, one kv head per GPU: capped at 256
+    assert split_factor(256, 8, 256, 148) == 1                    # 2048 units fill the GPU
+    assert split_factor(4, 8, 4096, 148) == 18                    # config 4, one GPU: 32 units x 18 = 576 CTAs
+    assert split_factor(4, 1, 4096, 148) == 148                   # config 4, one kv head per GPU
     assert split_factor(1, 1, 7, 148) == 1                        # too few pages to split
     assert split_factor(1, 1, 16, 148) == 4                       # >= 4 pages per split
-    for S, H, n in ((1, 1, 10 ** 6), (3, 5, 999)):
+    assert split_factor(1, 1, 10 ** 6, 148) == 256                # capped
+    for S, H, n in ((1, 1, 10 ** 6), (3, 5, 999), (64, 8, 8192)):
         ns = split_factor(S, H, n, 148)
-        assert ns & (ns - 1) == 0 and 1 <= ns <= 256
+        assert 1 <= ns <= 256 and (ns == 1 or n // ns >= 4)
 
 
 def test_dequant_helpers_roundtrip_on_cpu():
