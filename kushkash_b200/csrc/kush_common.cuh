@@ -65,13 +65,17 @@ __device__ __forceinline__ void qparams(float mn, float mx, float& s, float& b, 
     inv = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
 }
 
-// round((x - b) * inv) with ties to even (torch.round, as the reference's tests pin), clamped to the code range
+// round((x - b) * inv) with ties to even (torch.round, as the reference's tests pin), clamped to the code range.
+// The rounding is one fp32 add of 1.5 * 2^23: for |y| < 2^22 the sum's ulp is 1, so IEEE round-to-nearest-even of
+// the add is round-half-even of y, and the integer sits in the low mantissa bits (no float->int conversion op).
+// Larger |y| (only reachable if the inputs are not finite) saturate like the clamp.
 template <int BITS>
 __device__ __forceinline__ int qcode(float x, float b, float inv) {
-    constexpr float HALFF = float(1 << (BITS - 1));
-    float r = rintf(__fmul_rn(__fsub_rn(x, b), inv));
-    r = fminf(fmaxf(r, -HALFF), HALFF - 1.0f);
-    return int(r);
+    constexpr int HALF = 1 << (BITS - 1);
+    const float y = __fmul_rn(__fsub_rn(x, b), inv);
+    const float yc = fminf(fmaxf(y, -4194304.0f), 4194304.0f);
+    const int r = __float_as_int(__fadd_rn(yc, 12582912.0f)) - 0x4B400000;
+    return min(max(r, -HALF), HALF - 1);
 }
 
 __device__ __forceinline__ uint8_t pack4(int lo, int hi) { return uint8_t((lo & 0x0F) | ((hi & 0x0F) << 4)); }
