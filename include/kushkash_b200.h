@@ -107,10 +107,19 @@ int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void *out
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);
 
-/* Bounded-wait watchdog of the decode kernels: 1 if a decode launch gave up waiting for a page copy (its outputs
- * were written as NaN), else 0; clear != 0 resets the flag.  Synchronous (reads a device variable); -1 on a CUDA
- * error.  No counterpart in the reference, whose kernels have no bounded waits. */
+/* Bounded-wait watchdog of the kernels that wait on bulk copies: bit 0 set if a decode launch gave up waiting for a
+ * page copy (its outputs were written as NaN), bit 1 if a bulk write gave up waiting for its input rows (the
+ * records of that warp's remaining items were not written); 0 if neither.  clear != 0 resets both flags.
+ * Synchronous (reads device variables); -1 on a CUDA error.  No counterpart in the reference, whose kernels have
+ * no bounded waits. */
 int kush_sm100_device_error(int32_t clear);
+
+/* Exhaustive self-check of the bulk write's scale arithmetic on the current device: mismatches[0] / [1] = fp32
+ * values d in [2^-100, 2^100] for which the write's d / 15 / d / 255 (Markstein's correction step, scalar and
+ * fp32x2 forms) differs from the IEEE quotient, mismatches[2] = fp16 scales whose reciprocal (table of RN(1 / (1 + i / 1024)), scaled by a power
+ * of two) differs from the IEEE reciprocal.  All three are 0 on a correct build.  Synchronous; allocates 24 bytes
+ * of device memory.  No counterpart in the reference (a diagnostic of this implementation's arithmetic). */
+int kush_sm100_selfcheck(uint64_t *mismatches);
 
 /* Canonical Walsh-Hadamard rotation of `rows` rows of head_dim values: y[r] = fwht(x[r]) (row strides in
  * elements; y may alias x).  Replaces kush_fwht (kushkash/kush/gpu.mojo:95-112) as launched by Ops.fwht

@@ -41,6 +41,7 @@ SIGNATURES = {
                           _i64, _p, _i32, _p, _p, _i32, _p],
     "kush_sm100_record_bytes": [_i32, _i32, _i32],
     "kush_sm100_device_error": [_i32],
+    "kush_sm100_selfcheck": [_p],
     "kush_sm100_last_error": [],
     "kush_sm100_version": [],
 }
@@ -79,11 +80,20 @@ def check(rc: int, what: str) -> None:
 
 
 def device_error(clear: bool = True) -> int:
-    """1 if a decode launch gave up a bounded wait since the last clear (its outputs are NaN), else 0."""
+    """Bounded-wait flags since the last clear: bit 0 a decode launch gave up (its outputs are NaN), bit 1 a bulk
+    write gave up (some of its records were not written); 0 if neither."""
     rc = lib().kush_sm100_device_error(int(clear))
     if rc < 0:
         raise RuntimeError("kush_sm100_device_error: CUDA error")
     return rc
+
+
+def selfcheck() -> tuple[int, int, int]:
+    """Mismatch counts of the bulk write's scale arithmetic against IEEE division (levels 15, 255) and reciprocal,
+    checked exhaustively on the current device; (0, 0, 0) on a correct build."""
+    out = (ctypes.c_uint64 * 3)()
+    check(lib().kush_sm100_selfcheck(out), "kush_sm100_selfcheck")
+    return out[0], out[1], out[2]
 
 
 def raw_stream(device: int) -> int:

@@ -156,6 +156,9 @@ int set_error(int status, const char* fmt, ...);
 // checks the launch that just happened (cudaGetLastError); KUSH_OK or KUSH_ERR_CUDA with the message recorded
 int check_launch(const char* what);
 
+// the streaming write's bounded-wait flag (1 if a wait gave up), optionally cleared; -1 on a CUDA error
+int write_error_flag(int clear);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace kush

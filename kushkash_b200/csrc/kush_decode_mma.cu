@@ -22,23 +22,16 @@
 // the D dimension is permuted so every lane's fragments come from whole 32-bit words of its token rows.
 #include <stdio.h>
 
+#include "kush_async.cuh"
 #include "kush_common.cuh"
 
 namespace kush {
 
 constexpr int MMA_NW = 4;
-constexpr uint32_t WAIT_LIMIT = 1u << 26;      // try_wait polls before a wait is declared stuck
 
 __device__ int g_decode_error = 0;            // set when a bounded wait gave up (read by kush_sm100_device_error)
 
 // ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
 // (a & b) ^ c in one LOP3
 __device__ __forceinline__ uint32_t and_xor(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t r;
@@ -76,22 +69,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-// bounded wait on the mbarrier at shared address `bar` for phase parity `parity`
-__device__ __forceinline__ bool mbar_wait_u32(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
-        uint32_t ok;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-    }
-    return false;
-}
 // lane 0 of the warp (predicated, no branch): arm `bar` for `bytes` and start one 1-D bulk copy src -> dst (shared
 // addresses).  The slot's previous contents were read into registers and consumed by MMAs before this point in
 // program order, so no proxy fence is needed between those reads and the async-proxy write.
@@ -103,7 +80,6 @@ __device__ __forceinline__ void refill_lane0(uint32_t lane, uint32_t bar, uint32
         "r"(bar), "r"(dst), "r"(bytes), "l"(src)
         : "memory");
 }
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
 // fp16 constants as f16x2 words
 constexpr uint32_t H2_1032 = 0x64086408u;       // 1024 + 8: int4 low-nibble offset
@@ -672,5 +648,7 @@ extern "C" int kush_sm100_device_error(int32_t clear) {
         const int zero = 0;
         cudaMemcpyToSymbol(kush::g_decode_error, &zero, sizeof(int));
     }
-    return v;
+    const int w = kush::write_error_flag(clear);
+    if (w < 0) return -1;
+    return (v ? 1 : 0) | (w ? 2 : 0);
 }

@@ -7,6 +7,9 @@
 // stages a page's rows in shared memory with 16-byte loads and writes the assembled record with 16-byte stores.
 #include <stdio.h>
 
+#include <atomic>
+
+#include "kush_async.cuh"
 #include "kush_common.cuh"
 
 namespace kush {
@@ -44,12 +47,13 @@ __device__ __forceinline__ void quantize_v_row(const IN* __restrict__ src, uint8
 
 // K of one page by the threads of a block (kushkash/kush/gpu.mojo:121-160 _quantize_k_page): per-channel range
 // over the P tokens; token row t < split comes from ka + t*sa (the tail), the rest from kb + (t - split)*skb.
+// Thread `tid` of `nth` takes channels tid, tid + nth, ...
 template <int D, int BITS, int P, class IN>
 __device__ __forceinline__ void quantize_k_page(const IN* __restrict__ ka, int64_t sa, const IN* __restrict__ kb,
-                                                int64_t skb, int split, uint8_t* __restrict__ rec) {
+                                                int64_t skb, int split, uint8_t* __restrict__ rec, int tid, int nth) {
     using F = Fmt<D, BITS, P>;
     constexpr int NCH = BITS == 8 ? D : D / 2;             // threads with work: channel (int8) or channel pair (int4)
-    for (int c = threadIdx.x; c < NCH; c += blockDim.x) {
+    for (int c = tid; c < NCH; c += nth) {
         constexpr int NC = BITS == 8 ? 1 : 2;
         float bias[NC], inv[NC];
 #pragma unroll
@@ -105,7 +109,8 @@ __global__ void __launch_bounds__(D) append_kernel(const IN* __restrict__ k_new,
     if (slot == P - 1) {
         for (int h = 0; h < H; h++) {
             const IN* t0 = tail_k + tb + int64_t(h) * P * D;
-            quantize_k_page<D, BITS, P, IN>(t0, D, t0, D, P, rec_at(cache, blk, h, block_stride, head_stride));
+            quantize_k_page<D, BITS, P, IN>(t0, D, t0, D, P, rec_at(cache, blk, h, block_stride, head_stride),
+                                                threadIdx.x, blockDim.x);
         }
     }
     if (advance && d == 0) seq_lens[s] = int32_t(pos + 1);
@@ -276,6 +281,551 @@ __global__ void __launch_bounds__(D) write_kernel(const IN* __restrict__ k_new, 
     }
 }
 
+// ------------------------------------------------------------------ streaming bulk write (fp16 / bf16 inputs)
+// The ragged write again, as a persistent kernel: every warp owns a stream of (job, kv head) items (item = job * H +
+// head; warp g of the grid takes items g, g + W, g + 2W, ...) and a ring of NS shared-memory slots.  An item whose
+// page is entirely new and complete (every page of a prefill chunk but its first and last) is a "full" item: its P
+// K rows and P V rows are brought into a slot by 2P one-row bulk copies (cp.async.bulk, mbarrier completion, no
+// multicast), issued NS - 1 items ahead, and encoded from there with packed arithmetic straight into the record
+// (16-bit min / max on the raw inputs, fp32x2 code arithmetic, byte packing with IMAD / PRMT, 4 to 16-byte stores).
+// Other items (a page that continues the old tail, a sequence's last partial page, mode 1) take the warp-level
+// version of the per-token path above.  Job metadata (sequence, page, offsets, block id) is prefetched 32 items at a
+// time, one item per lane.
+//
+// Scale arithmetic, bit-exact with qparams: (mx - mn) / (2^BITS - 1) by Markstein's correction step (q0 = d * R,
+// r = fma(-q0, L, d), q = fma(r, R, q0) with R = RN(1 / L): the correctly rounded quotient when q0 is within an ulp
+// and nothing under- or overflows; other d take the IEEE divide), and 1 / s from a table of RN(1 / (1 + i / 1024)):
+// every fp16 value s is m * 2^e with a 10-bit fraction, so RN(1 / s) = RN(1 / m) * 2^-e exactly.
+__device__ int g_write_error = 0;              // set when a bounded wait of the streaming write gave up
+
+template <class IN> struct Pair16;
+template <> struct Pair16<__nv_bfloat16> {
+    static __device__ __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
+    static __device__ __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+    static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
+        uint32_t r;
+        asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+        return r;
+    }
+    static __device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+        uint32_t r;
+        asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+        return r;
+    }
+};
+template <> struct Pair16<__half> {
+    static __device__ __forceinline__ float lo(uint32_t w) { return __half2float(__ushort_as_half(uint16_t(w))); }
+    static __device__ __forceinline__ float hi(uint32_t w) { return __half2float(__ushort_as_half(uint16_t(w >> 16))); }
+    static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
+        uint32_t r;
+        asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+        return r;
+    }
+    static __device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+        uint32_t r;
+        asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+        return r;
+    }
+};
+
+// (mx - mn) / (2^BITS - 1), correctly rounded (Markstein), IEEE divide outside [2^-100, 2^100]
+template <int BITS>
+__device__ __forceinline__ float div_levels(float d) {
+    constexpr float L = float((1 << BITS) - 1);
+    constexpr float R = 1.0f / L;
+    const float q0 = __fmul_rn(d, R);
+    float q = __fmaf_rn(__fmaf_rn(-q0, L, d), R, q0);
+    if (!(d <= 0x1p100f && (d >= 0x1p-100f || d == 0.0f))) q = __fdiv_rn(d, L);
+    return q;
+}
+
+// RN(1 / s) for an fp16-representable s (s > 0 and finite), else 0 -- qparams' `s > 0 ? 1 / s : 0`
+__device__ __forceinline__ float rcp_fp16(float s, const uint32_t* T) {
+    const uint32_t sb = __float_as_uint(s);
+    const uint32_t v = T[(sb >> 13) & 1023u] - (sb & 0x7f800000u) + 0x3f800000u;
+    return (s > 0.0f && s <= 65504.0f) ? __uint_as_float(v) : 0.0f;
+}
+
+// fp32x2 arithmetic of the scale and code paths (PTX with explicit rounding).  One measured hazard on sm_100a: a
+// packed multiply whose result feeds a packed add directly could come out rounded once, as by one fused
+// multiply-add, even with -fmad=false; the magic add after the code multiply is therefore two scalar __fadd_rn.
+__device__ __forceinline__ uint64_t f2_bits(float2 a) {
+    return uint64_t(__float_as_uint(a.x)) | uint64_t(__float_as_uint(a.y)) << 32;
+}
+__device__ __forceinline__ float2 bits_f2(uint64_t r) {
+    return make_float2(__uint_as_float(uint32_t(r)), __uint_as_float(uint32_t(r >> 32)));
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(r);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(r);
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return bits_f2(r);
+}
+
+// div_levels for two values at once (the form the write kernel uses)
+template <int BITS>
+__device__ __forceinline__ float2 div_levels2(float2 d) {
+    constexpr float L = float((1 << BITS) - 1), R = 1.0f / L;
+    const float2 q0 = mul2_rn(d, make_float2(R, R));
+    float2 q = fma2_rn(fma2_rn(q0, make_float2(-L, -L), d), make_float2(R, R), q0);
+    if (!(d.x <= 0x1p100f && (d.x >= 0x1p-100f || d.x == 0.0f))) q.x = __fdiv_rn(d.x, L);
+    if (!(d.y <= 0x1p100f && (d.y >= 0x1p-100f || d.y == 0.0f))) q.y = __fdiv_rn(d.y, L);
+    return q;
+}
+
+// qparams for two ranges at once (x: first, y: second), fp32x2 arithmetic; also returns the fp16 scales and biases
+// as half2 bits and whether any value of either range can need qcode's clamp: the code of a value is monotone in
+// it, so when the codes of both ends (mn, mx) are inside the code range, every code is.
+template <int BITS>
+__device__ __forceinline__ bool qparams2(float2 mn, float2 mx, const uint32_t* T, uint32_t& sh2, uint32_t& bh2,
+                                         float2& b, float2& inv) {
+    constexpr float HALFF = float(1 << (BITS - 1));
+    constexpr float LO = -HALFF - 0.5f, HI = HALFF - 0.5f;          // round(y) in range <=> LO <= y < HI
+    const float2 m1 = make_float2(-1.0f, -1.0f);
+    const float2 d = fma2_rn(mn, m1, mx);                       // mx - mn
+    const float2 q = div_levels2<BITS>(d);
+    const __half2 s16 = __floats2half2_rn(q.x, q.y);
+    const float2 s = __half22float2(s16);
+    const float2 bp = fma2_rn(s, make_float2(HALFF, HALFF), mn);   // mn + s * HALF (the product is exact)
+    const __half2 b16 = __floats2half2_rn(bp.x, bp.y);
+    b = __half22float2(b16);
+    inv = make_float2(rcp_fp16(s.x, T), rcp_fp16(s.y, T));
+    sh2 = *reinterpret_cast<const uint32_t*>(&s16);
+    bh2 = *reinterpret_cast<const uint32_t*>(&b16);
+    const float2 ylo = mul2_rn(fma2_rn(b, m1, mn), inv), yhi = mul2_rn(fma2_rn(b, m1, mx), inv);
+    return !(ylo.x >= LO && ylo.y >= LO && yhi.x < HI && yhi.y < HI);
+}
+
+// codes of a pair of values (x.x, x.y) against their (bias, 1 / scale) pairs: float bits whose low byte is the code
+// (int8: two's complement; int4: code + 8), by qcode's round-half-even magic add; CL: with qcode's clamp (taken
+// before the rounding: rounding is monotone and the bounds are integers, so the codes are the same)
+template <int BITS, bool CL>
+__device__ __forceinline__ uint2 code_bits(float2 x, float2 b, float2 iv) {
+    constexpr float LO = -float(1 << (BITS - 1)), HI = float((1 << (BITS - 1)) - 1);
+    constexpr float MAGIC = BITS == 4 ? 12582920.0f : 12582912.0f;       // 1.5 * 2^23 (+ 8)
+    float2 y = mul2_rn(fma2_rn(b, make_float2(-1.0f, -1.0f), x), iv);
+    if constexpr (CL) {
+        y.x = fminf(fmaxf(y.x, LO), HI);
+        y.y = fminf(fmaxf(y.y, LO), HI);
+    }
+    return make_uint2(__float_as_uint(__fadd_rn(y.x, MAGIC)), __float_as_uint(__fadd_rn(y.y, MAGIC)));
+}
+
+template <class IN> __device__ __forceinline__ float2 f2_of(uint32_t w) {
+    return make_float2(Pair16<IN>::lo(w), Pair16<IN>::hi(w));
+}
+
+// int4: two code bytes (bits 0-15, each still XOR 0x88) of lo dims (a.lo, a.hi) and hi dims (b.lo, b.hi)
+template <class IN, bool CL>
+__device__ __forceinline__ uint32_t unit4(uint32_t a, uint32_t b, float2 b0, float2 iv0, float2 b1, float2 iv1) {
+    const float2 fa = f2_of<IN>(a), fb = f2_of<IN>(b);
+    const uint2 e0 = code_bits<4, CL>(make_float2(fa.x, fb.x), b0, iv0);
+    const uint2 e1 = code_bits<4, CL>(make_float2(fa.y, fb.y), b1, iv1);
+    return prmt(e0.y * 16u + e0.x, e1.y * 16u + e1.x, 0x0040);          // low byte: (lo + 8) | (hi + 8) << 4
+}
+// int8: two code bytes (bits 0-15) of dims (a.lo, a.hi)
+template <class IN, bool CL>
+__device__ __forceinline__ uint32_t unit8(uint32_t a, float2 b, float2 iv) {
+    const uint2 e = code_bits<8, CL>(f2_of<IN>(a), b, iv);
+    return prmt(e.x, e.y, 0x0040);
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+template <int D, int BITS, int P, class IN>
+struct WS {
+    using F = Fmt<D, BITS, P>;
+    static constexpr int ROWB = 2 * D;                              // bytes of an input row
+    static constexpr int STAGE = 2 * P * ROWB;                      // one slot: P K rows, then P V rows
+    static constexpr int NS = 2;                                    // ring slots per warp
+    static constexpr int NW = STAGE <= 8192 ? 4 : 2;                // warps per CTA
+    static constexpr int OFF_BAR = 4096;                            // after the 1024-entry reciprocal table
+    static constexpr int OFF_STAGE = OFF_BAR + 128;
+    static constexpr int SMEM = OFF_STAGE + NW * NS * STAGE;
+    // V: GL lanes per row (16 values each), RPB rows per pass; passes go in pairs (2 rows per lane)
+    static constexpr int GL = D / 16, RPB = 32 / GL;
+    // K: lane = KC code bytes of a row (int4: KC lo dims + KC hi dims; int8: KC dims), LW lanes per token set,
+    // TS token sets of TPS rows (ranges combined across sets by shuffles)
+    static constexpr int DC = F::DC;
+    static constexpr int KC = DC / 32 > 4 ? DC / 32 : 4;
+    static constexpr int LW = DC / KC, TS = 32 / LW, TPS = P / TS;
+    static constexpr int NU = KC / 2;                               // 2-byte code units per row per lane
+    static constexpr int KWD = BITS == 4 ? KC : KC / 2;             // input words per row per lane
+    static constexpr int NPR = BITS == 4 ? 2 * NU : NU;             // channel pairs per lane
+    static constexpr bool KREG = TPS * KWD <= 32;                   // keep the K words in registers between passes
+    static_assert((P / RPB) % 2 == 0, "V passes go in pairs");
+};
+
+// 16 V values of row r for lane g: int4: lo dims [8g, 8g + 8) and hi dims D/2 + [8g, 8g + 8) (code bytes
+// [8g, 8g + 8)); int8: dims [16g, 16g + 16) (code bytes [16g, 16g + 16))
+template <int D, int BITS>
+__device__ __forceinline__ void v_words(const uint8_t* row, int g, uint32_t (&w)[8]) {
+    const uint4 a = lds128(row + (BITS == 4 ? 16 * g : 32 * g));
+    const uint4 b = lds128(row + (BITS == 4 ? D + 16 * g : 32 * g + 16));
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+
+template <int D, int BITS, int P, class IN, bool CL>
+__device__ __forceinline__ void v_encode(const uint32_t (&w)[8], float bias, float inv, uint8_t* dst, int g) {
+    const float2 b = make_float2(bias, bias), iv = make_float2(inv, inv);
+    if constexpr (BITS == 4) {
+        uint32_t o[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+            o[k] = prmt(unit4<IN, CL>(w[2 * k], w[4 + 2 * k], b, iv, b, iv),
+                        unit4<IN, CL>(w[2 * k + 1], w[5 + 2 * k], b, iv, b, iv), 0x5410) ^ 0x88888888u;
+        *reinterpret_cast<uint2*>(dst + 8 * g) = make_uint2(o[0], o[1]);
+    } else {
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            o[k] = prmt(unit8<IN, CL>(w[2 * k], b, iv), unit8<IN, CL>(w[2 * k + 1], b, iv), 0x5410);
+        *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// (min, -max) of a row's values in one 16-bit pair word, reduced over the GL lanes of the row
+template <class IN, int GL>
+__device__ __forceinline__ uint32_t row_range(const uint32_t (&w)[8]) {
+    using PR = Pair16<IN>;
+    const uint32_t m = PR::min2(PR::min2(PR::min2(w[0], w[1]), PR::min2(w[2], w[3])),
+                                PR::min2(PR::min2(w[4], w[5]), PR::min2(w[6], w[7])));
+    const uint32_t M = PR::max2(PR::max2(PR::max2(w[0], w[1]), PR::max2(w[2], w[3])),
+                                PR::max2(PR::max2(w[4], w[5]), PR::max2(w[6], w[7])));
+    const uint32_t nM = M ^ 0x80008000u;                            // -max: both ranges reduce as one min
+    uint32_t mm = PR::min2(prmt(m, nM, 0x5410), prmt(m, nM, 0x7632));
+#pragma unroll
+    for (int o = GL / 2; o; o >>= 1) mm = PR::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    return mm;
+}
+
+// V rows of a full page from the slot, two rows per lane at a time: rows 2p RPB + lane / GL and (2p + 1) RPB + lane / GL
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, const uint32_t* T, int lane) {
+    using C = WS<D, BITS, P, IN>;
+    using F = typename C::F;
+    using PR = Pair16<IN>;
+    const int g = lane % C::GL;
+#pragma unroll 1
+    for (int pp = 0; pp < P / C::RPB / 2; pp++) {
+        const int r0 = 2 * pp * C::RPB + lane / C::GL, r1 = r0 + C::RPB;
+        uint32_t w0[8], w1[8];
+        v_words<D, BITS>(vbuf + r0 * C::ROWB, g, w0);
+        v_words<D, BITS>(vbuf + r1 * C::ROWB, g, w1);
+        const uint32_t mm0 = row_range<IN, C::GL>(w0), mm1 = row_range<IN, C::GL>(w1);
+        uint32_t sh2, bh2;
+        float2 b, inv;
+        const bool need = qparams2<BITS>(make_float2(PR::lo(mm0), PR::lo(mm1)), make_float2(-PR::hi(mm0), -PR::hi(mm1)),
+                                         T, sh2, bh2, b, inv);
+        if (g == 0) {
+            uint16_t* vs = reinterpret_cast<uint16_t*>(rec + F::OFF_VS);
+            uint16_t* vb = reinterpret_cast<uint16_t*>(rec + F::OFF_VB);
+            vs[r0] = uint16_t(sh2);
+            vs[r1] = uint16_t(sh2 >> 16);
+            vb[r0] = uint16_t(bh2);
+            vb[r1] = uint16_t(bh2 >> 16);
+        }
+        uint8_t* q = rec + F::OFF_VQ;
+        if (__any_sync(0xffffffffu, need)) {
+            v_encode<D, BITS, P, IN, true>(w0, b.x, inv.x, q + r0 * F::DC, g);
+            v_encode<D, BITS, P, IN, true>(w1, b.y, inv.y, q + r1 * F::DC, g);
+        } else {
+            v_encode<D, BITS, P, IN, false>(w0, b.x, inv.x, q + r0 * F::DC, g);
+            v_encode<D, BITS, P, IN, false>(w1, b.y, inv.y, q + r1 * F::DC, g);
+        }
+    }
+}
+
+// this lane's K input words of row t: int4: KC/2 words of lo dims [c KC, c KC + KC), then the same of hi dims;
+// int8: KC/2 words of dims [c KC, c KC + KC)
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void ws_k_words(const uint8_t* kbuf, int t, int c, uint32_t (&w)[WS<D, BITS, P, IN>::KWD]) {
+    using C = WS<D, BITS, P, IN>;
+    const uint8_t* row = kbuf + t * C::ROWB + 2 * c * C::KC;
+    if constexpr (C::KC == 4) {
+        const uint2 a = *reinterpret_cast<const uint2*>(row);
+        w[0] = a.x;
+        w[1] = a.y;
+        if constexpr (BITS == 4) {
+            const uint2 b = *reinterpret_cast<const uint2*>(row + D);
+            w[2] = b.x;
+            w[3] = b.y;
+        }
+    } else {                                                         // int8, KC = 8
+        const uint4 a = lds128(row);
+        w[0] = a.x;
+        w[1] = a.y;
+        w[2] = a.z;
+        w[3] = a.w;
+    }
+}
+
+template <int D, int BITS, int P, class IN, bool CL>
+__device__ __forceinline__ void k_encode(const uint32_t (&w)[WS<D, BITS, P, IN>::KWD], const float2 (&b)[WS<D, BITS, P, IN>::NPR],
+                                         const float2 (&iv)[WS<D, BITS, P, IN>::NPR], uint8_t* dst) {
+    using C = WS<D, BITS, P, IN>;
+    constexpr int NU = C::NU;
+    uint32_t u16[NU];
+#pragma unroll
+    for (int u = 0; u < NU; u++) {
+        if constexpr (BITS == 4) u16[u] = unit4<IN, CL>(w[u], w[NU + u], b[2 * u], iv[2 * u], b[2 * u + 1], iv[2 * u + 1]);
+        else u16[u] = unit8<IN, CL>(w[u], b[u], iv[u]);
+    }
+    if constexpr (NU == 2) {
+        uint32_t o = prmt(u16[0], u16[1], 0x5410);
+        if constexpr (BITS == 4) o ^= 0x88888888u;
+        *reinterpret_cast<uint32_t*>(dst) = o;
+    } else {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(prmt(u16[0], u16[1], 0x5410), prmt(u16[2], u16[3], 0x5410));
+    }
+}
+
+// K of a full page from the slot: per-channel ranges over the P rows, then the codes
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, const uint32_t* T, int lane) {
+    using C = WS<D, BITS, P, IN>;
+    using F = typename C::F;
+    using PR = Pair16<IN>;
+    constexpr int KWD = C::KWD, NU = C::NU, NPR = C::NPR;
+    constexpr int TR = C::KREG ? C::TPS : 1;                         // rows whose words stay in registers
+    const int c = lane % C::LW, t0 = (lane / C::LW) * C::TPS;
+    uint32_t kw[TR][KWD];
+    uint32_t mn[KWD], mx[KWD];
+    ws_k_words<D, BITS, P, IN>(kbuf, t0, c, kw[0]);
+#pragma unroll
+    for (int i = 0; i < KWD; i++) mn[i] = mx[i] = kw[0][i];
+#pragma unroll
+    for (int t = 1; t < C::TPS; t++) {
+        uint32_t w[KWD];
+        ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, c, w);
+#pragma unroll
+        for (int i = 0; i < KWD; i++) {
+            if constexpr (C::KREG) kw[t < TR ? t : 0][i] = w[i];
+            mn[i] = PR::min2(mn[i], w[i]);
+            mx[i] = PR::max2(mx[i], w[i]);
+        }
+    }
+#pragma unroll
+    for (int o = C::LW; o < 32; o <<= 1)
+#pragma unroll
+        for (int i = 0; i < KWD; i++) {
+            mn[i] = PR::min2(mn[i], __shfl_xor_sync(0xffffffffu, mn[i], o));
+            mx[i] = PR::max2(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
+        }
+    // channel pairs: int4 pair 2u + p = (lo dim 2u + p, hi dim 2u + p) of the lane; int8 pair u = (dim 2u, 2u + 1)
+    float2 b[NPR], iv[NPR];
+    uint32_t sh[NPR], bh[NPR];
+    bool need = false;
+#pragma unroll
+    for (int pr = 0; pr < NPR; pr++) {
+        float2 lo_, hi_;
+        if constexpr (BITS == 4) {
+            const int u = pr / 2;
+            const bool up = pr & 1;
+            lo_ = make_float2(up ? PR::hi(mn[u]) : PR::lo(mn[u]), up ? PR::hi(mn[NU + u]) : PR::lo(mn[NU + u]));
+            hi_ = make_float2(up ? PR::hi(mx[u]) : PR::lo(mx[u]), up ? PR::hi(mx[NU + u]) : PR::lo(mx[NU + u]));
+        } else {
+            lo_ = f2_of<IN>(mn[pr]);
+            hi_ = f2_of<IN>(mx[pr]);
+        }
+        need |= qparams2<BITS>(lo_, hi_, T, sh[pr], bh[pr], b[pr], iv[pr]);
+    }
+    if (lane < C::LW) {                                  // token set 0 stores the scales and biases
+        if constexpr (BITS == 4) {
+            static_assert(NU == 2, "int4 lanes hold 4 lo + 4 hi dims");
+            // unit u: lo dims (2u, 2u + 1) = low halves of pairs 2u, 2u + 1; hi dims = their high halves
+            const uint2 s_lo = make_uint2(prmt(sh[0], sh[1], 0x5410), prmt(sh[2], sh[3], 0x5410));
+            const uint2 s_hi = make_uint2(prmt(sh[0], sh[1], 0x7632), prmt(sh[2], sh[3], 0x7632));
+            const uint2 b_lo = make_uint2(prmt(bh[0], bh[1], 0x5410), prmt(bh[2], bh[3], 0x5410));
+            const uint2 b_hi = make_uint2(prmt(bh[0], bh[1], 0x7632), prmt(bh[2], bh[3], 0x7632));
+            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * c * C::KC) = s_lo;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KS + D + 2 * c * C::KC) = s_hi;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * c * C::KC) = b_lo;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KB + D + 2 * c * C::KC) = b_hi;
+        } else if constexpr (NU == 2) {
+            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * c * C::KC) = make_uint2(sh[0], sh[1]);
+            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * c * C::KC) = make_uint2(bh[0], bh[1]);
+        } else {
+            *reinterpret_cast<uint4*>(rec + F::OFF_KS + 2 * c * C::KC) = make_uint4(sh[0], sh[1], sh[2], sh[3]);
+            *reinterpret_cast<uint4*>(rec + F::OFF_KB + 2 * c * C::KC) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
+        }
+    }
+    uint8_t* dst = rec + t0 * F::DC + c * C::KC;
+    const bool cl = __any_sync(0xffffffffu, need);
+#pragma unroll
+    for (int t = 0; t < C::TPS; t++) {
+        uint32_t w[KWD];
+        if constexpr (C::KREG) {
+#pragma unroll
+            for (int i = 0; i < KWD; i++) w[i] = kw[t][i];
+        } else {
+            ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, c, w);
+        }
+        if (cl) k_encode<D, BITS, P, IN, true>(w, b, iv, dst + t * F::DC);
+        else k_encode<D, BITS, P, IN, false>(w, b, iv, dst + t * F::DC);
+    }
+}
+
+// job metadata of one item, one item per lane (see write_stream_kernel); hf = kv head | full << 30
+struct WMeta {
+    int row0, hf, blk, s, pg, q0, ctx, total;
+};
+
+template <int D, int BITS, int P, class IN>
+__global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
+    write_stream_kernel(const IN* __restrict__ k_new, const IN* __restrict__ v_new, int64_t k_stride, int64_t v_stride,
+                        const int32_t* __restrict__ qsl, const int32_t* __restrict__ seq_lens,
+                        const int32_t* __restrict__ tail_idx, const int32_t* __restrict__ job_seq,
+                        const int32_t* __restrict__ job_page, int mode, uint8_t* cache, int64_t block_stride,
+                        int64_t head_stride, IN* tail_k, const int32_t* __restrict__ block_table, int64_t max_pages,
+                        int H, int n_jobs) {
+    using C = WS<D, BITS, P, IN>;
+    constexpr int FULL = 1 << 30;
+    extern __shared__ __align__(128) uint8_t wsm[];
+    uint32_t* T = reinterpret_cast<uint32_t*>(wsm);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wsm + C::OFF_BAR);
+    const int lane = threadIdx.x % WARP, w = threadIdx.x / WARP;
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+        T[i] = __float_as_uint(__frcp_rn(1.0f + float(i) * (1.0f / 1024.0f)));
+    if (threadIdx.x < C::NW * C::NS) mbar_init(&bars[threadIdx.x], 1);
+    fence_mbar_init();
+    __syncthreads();
+
+    uint8_t* slots = wsm + C::OFF_STAGE + w * C::NS * C::STAGE;
+    const uint32_t bar0 = smem_u32(&bars[w * C::NS]);
+    const int64_t n_items = int64_t(n_jobs) * H;
+    const int64_t TW = int64_t(gridDim.x) * C::NW;
+    const int64_t first = int64_t(blockIdx.x) * C::NW + w;
+    const int n_local = first < n_items ? int((n_items - first + TW - 1) / TW) : 0;
+
+    auto load_meta = [&](int batch) {
+        WMeta m{0, 0, 0, 0, 0, 0, 0, 0};
+        const int64_t it = first + (int64_t(batch) * WARP + lane) * TW;
+        if (it < n_items) {
+            const int64_t j = it / H;
+            m.s = job_seq[j];
+            m.pg = job_page[j];
+            m.q0 = qsl[m.s];
+            m.total = seq_lens[m.s];
+            m.ctx = m.total - (qsl[m.s + 1] - m.q0);
+            m.blk = block_table[int64_t(m.s) * max_pages + m.pg];
+            const int ps = m.pg * P;
+            m.row0 = m.q0 + ps - m.ctx;
+            const bool full = mode != 1 && ps >= m.ctx && ps + P <= m.total;
+            m.hf = int(it - j * H) | (full ? FULL : 0);
+        }
+        return m;
+    };
+    WMeta cur = load_meta(0), nxt = load_meta(1);
+#define KUSH_META(field, use_b, l) __shfl_sync(0xffffffffu, (use_b) ? nxt.field : cur.field, (l))
+    // bring the rows of full item i (first input row row0, kv head h) into slot i % NS
+    auto issue = [&](int i, int row0, int h) {
+        const uint32_t bar = bar0 + 8u * uint32_t(i % C::NS);
+        const uint32_t dst = smem_u32(slots + (i % C::NS) * C::STAGE);
+        if (lane == 0)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(uint32_t(C::STAGE))
+                         : "memory");
+        __syncwarp();
+#pragma unroll
+        for (int r = lane; r < 2 * P; r += WARP) {
+            const IN* src = r < P ? k_new + (int64_t(row0) + r) * k_stride + int64_t(h) * D
+                                  : v_new + (int64_t(row0) + r - P) * v_stride + int64_t(h) * D;
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                             dst + uint32_t(r * C::ROWB)),
+                         "l"(src), "r"(uint32_t(C::ROWB)), "r"(bar)
+                         : "memory");
+        }
+    };
+    // every other item: the warp-level per-token path (mode 0 / 1 / 2 as write_kernel), slot i % NS as scratch
+    auto general = [&](int i, int l, int h, int blk) {
+        const int64_t ps = int64_t(KUSH_META(pg, false, l)) * P, ctx = KUSH_META(ctx, false, l);
+        const int64_t total = KUSH_META(total, false, l), q0 = KUSH_META(q0, false, l);
+        const int s = KUSH_META(s, false, l);
+        const int64_t tb = (int64_t(tail_idx[s]) * H + h) * P * D;
+        const bool complete = ps + P <= total;
+        auto stash = [&](int64_t pstart) {
+            for (int64_t t = max(pstart, ctx); t < total; t++)
+                for (int d = lane; d < D; d += WARP)
+                    tail_k[tb + (t - pstart) * D + d] = k_new[(q0 + t - ctx) * k_stride + int64_t(h) * D + d];
+        };
+        if (mode == 1) {
+            if (!complete) stash(ps);
+            return;
+        }
+        uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
+        const int r0 = int(max(ps, ctx) - ps), r1 = int(min(ps + P, total) - ps);
+        const int split = complete ? int(max(int64_t(0), min(int64_t(P), ctx - ps))) : 0;
+        IN* kold = reinterpret_cast<IN*>(slots + (i % C::NS) * C::STAGE);        // [split][D] old tail rows
+        for (int e = lane; e < split * D; e += WARP) kold[e] = tail_k[tb + e];
+        __syncwarp();
+        if (mode == 2) {
+            const int64_t f0 = (ctx / P) * P, last = ((total - 1) / P) * P;
+            const bool last_partial = total % P != 0 && total > ctx;
+            const bool first_reads_tail = ctx % P != 0 && f0 + P <= total;
+            if (last_partial && ((first_reads_tail && last != f0) ? ps == f0 : ps == last)) stash(last);
+        }
+        for (int r = r0; r < r1; r++)
+            quantize_v_row<D, BITS, P, IN>(v_new + (q0 + ps + r - ctx) * v_stride + int64_t(h) * D, rec, r, lane);
+        if (complete)
+            quantize_k_page<D, BITS, P, IN>(kold, D, k_new + (q0 + ps + split - ctx) * k_stride + int64_t(h) * D,
+                                            k_stride, split, rec, lane, WARP);
+        __syncwarp();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the slot may next be filled by a bulk copy
+    };
+
+    for (int i = 0; i < C::NS - 1 && i < n_local; i++) {
+        const int hf = KUSH_META(hf, false, i);
+        if (hf & FULL) issue(i, KUSH_META(row0, false, i), hf & (FULL - 1));
+    }
+    uint32_t phase = 0;
+    for (int i = 0; i < n_local; i++) {
+        if (i % WARP == 0 && i) {
+            cur = nxt;
+            nxt = load_meta(i / WARP + 1);
+        }
+        const int ia = i + C::NS - 1;                                // the item whose rows start now
+        if (ia < n_local) {
+            const bool nb = ia / WARP != i / WARP;
+            const int hfa = KUSH_META(hf, nb, ia % WARP);
+            if (hfa & FULL) issue(ia, KUSH_META(row0, nb, ia % WARP), hfa & (FULL - 1));
+        }
+        const int l = i % WARP;
+        const int hf = KUSH_META(hf, false, l), blk = KUSH_META(blk, false, l);
+        const int h = hf & (FULL - 1), slot = i % C::NS;
+        if (hf & FULL) {
+            if (!__all_sync(0xffffffffu, mbar_wait_u32(bar0 + 8u * slot, (phase >> slot) & 1u))) {
+                // a copy never completed: record it, wait (bounded) for this warp's other copies, stop
+                if (lane == 0) atomicExch(&g_write_error, 1);
+                for (int k = i + 1; k < i + C::NS && k < n_local; k++) {
+                    const int sk = k % C::NS;
+                    if (KUSH_META(hf, k / WARP != i / WARP, k % WARP) & FULL)
+                        mbar_wait_u32(bar0 + 8u * sk, (phase >> sk) & 1u);
+                }
+                return;
+            }
+            phase ^= 1u << slot;
+            const uint8_t* kbuf = slots + slot * C::STAGE;
+            uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
+            ws_v_rows<D, BITS, P, IN>(kbuf + P * C::ROWB, rec, T, lane);
+            ws_k_page<D, BITS, P, IN>(kbuf, rec, T, lane);
+        } else {
+            general(i, l, h, blk);
+        }
+        __syncwarp();
+    }
+#undef KUSH_META
+}
+
 template <int D, int BITS, int P, class IN>
 int launch_append(const void* k_new, const void* v_new, int64_t k_stride, int64_t v_stride, int32_t* seq_lens,
                   int32_t pos_offset, int32_t advance, const int32_t* tail_idx, void* cache, int64_t block_stride,
@@ -286,6 +836,37 @@ int launch_append(const void* k_new, const void* v_new, int64_t k_stride, int64_
         tail_idx, static_cast<uint8_t*>(cache), block_stride, head_stride, static_cast<IN*>(tail_k), block_table,
         max_pages, hkv);
     return check_launch("kush_sm100_append");
+}
+
+// the streaming write: grid = resident CTAs of the device (or fewer when there are fewer items than warps)
+template <int D, int BITS, int P, class IN>
+int launch_write_stream(const void* k_new, const void* v_new, int64_t k_stride, int64_t v_stride, const int32_t* qsl,
+                        const int32_t* seq_lens, const int32_t* tail_idx, const int32_t* job_seq,
+                        const int32_t* job_page, int32_t mode, void* cache, int64_t block_stride, int64_t head_stride,
+                        void* tail_k, const int32_t* block_table, int64_t max_pages, int32_t hkv, int32_t n_jobs,
+                        int dev, cudaStream_t stream) {
+    using C = WS<D, BITS, P, IN>;
+    auto kern = write_stream_kernel<D, BITS, P, IN>;
+    static std::atomic<int> resident[64];                // per device: CTAs per SM x SMs, 0 until first use
+    const int di = dev & 63;
+    int slots = resident[di].load(std::memory_order_relaxed);
+    if (slots == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        int per_sm = 0, sms = 0;
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, C::NW * WARP, C::SMEM);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "write: kernel setup: %s", cudaGetErrorString(e));
+        if (per_sm < 1) return set_error(KUSH_ERR_CUDA, "write: streaming kernel does not fit on an SM");
+        slots = per_sm * sms;
+        resident[di].store(slots, std::memory_order_relaxed);
+    }
+    const int64_t want = (int64_t(n_jobs) * hkv + C::NW - 1) / C::NW;
+    const int grid = int(want < slots ? want : slots);
+    kern<<<grid, C::NW * WARP, C::SMEM, stream>>>(
+        static_cast<const IN*>(k_new), static_cast<const IN*>(v_new), k_stride, v_stride, qsl, seq_lens, tail_idx,
+        job_seq, job_page, mode, static_cast<uint8_t*>(cache), block_stride, head_stride, static_cast<IN*>(tail_k),
+        block_table, max_pages, hkv, n_jobs);
+    return check_launch("kush_sm100_write");
 }
 
 template <int D, int BITS, int P, class IN>
@@ -309,12 +890,64 @@ int launch_write(const void* k_new, const void* v_new, int64_t k_stride, int64_t
     const int vin = al(k_new) && al(v_new) && al(tail_k) && (k_stride * int64_t(sizeof(IN))) % 16 == 0 &&
                     (v_stride * int64_t(sizeof(IN))) % 16 == 0;
     const int vout = al(cache) && block_stride % 16 == 0 && head_stride % 16 == 0;     // 16-byte record stores
+    if constexpr (sizeof(IN) == 2) {
+        if (vin && vout)
+            return launch_write_stream<D, BITS, P, IN>(k_new, v_new, k_stride, v_stride, qsl, seq_lens, tail_idx,
+                                                       job_seq, job_page, mode, cache, block_stride, head_stride,
+                                                       tail_k, block_table, max_pages, hkv, n_jobs, dev, stream);
+    }
     const int vec = vin | (vout << 1);
     kern<<<grid, D, smem, stream>>>(
         static_cast<const IN*>(k_new), static_cast<const IN*>(v_new), k_stride, v_stride, qsl, seq_lens, tail_idx,
         job_seq, job_page, mode, static_cast<uint8_t*>(cache), block_stride, head_stride, static_cast<IN*>(tail_k),
         block_table, max_pages, hkv, vec);
     return check_launch("kush_sm100_write");
+}
+
+// Exhaustive check of the scale arithmetic of the streaming write against CUDA's IEEE operations: div_levels and
+// the packed div_levels2 (every value through both lanes) for every fp32 d in [2^-100, 2^100] (and 0), BITS 4 and
+// 8, against __fdiv_rn; rcp_fp16 for every fp16 bit pattern against `s > 0 ? __frcp_rn(s) : 0`.  Mismatch counts in
+// bad[0..2].
+__global__ void __launch_bounds__(256) selfcheck_kernel(unsigned long long* bad) {
+    __shared__ uint32_t T[1024];
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+        T[i] = __float_as_uint(__frcp_rn(1.0f + float(i) * (1.0f / 1024.0f)));
+    __syncthreads();
+    const uint32_t lo = 0x0D800000u, hi = 0x71800000u;          // 2^-100 .. 2^100
+    unsigned long long b4 = 0, b8 = 0, br = 0;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t u = lo + blockIdx.x * blockDim.x + threadIdx.x; u <= hi; u += stride) {
+        // d in the first lane of the packed form, its neighbour in the other (every value goes through both lanes)
+        const float d = __uint_as_float(u), e = __uint_as_float(u > lo ? u - 1 : hi);
+        const float q4 = __fdiv_rn(d, 15.0f), q8 = __fdiv_rn(d, 255.0f);
+        const float2 p4 = div_levels2<4>(make_float2(d, e)), p8 = div_levels2<8>(make_float2(e, d));
+        b4 += (__float_as_uint(div_levels<4>(d)) != __float_as_uint(q4)) + (__float_as_uint(p4.x) != __float_as_uint(q4)) +
+              (__float_as_uint(p4.y) != __float_as_uint(__fdiv_rn(e, 15.0f)));
+        b8 += (__float_as_uint(div_levels<8>(d)) != __float_as_uint(q8)) + (__float_as_uint(p8.y) != __float_as_uint(q8)) +
+              (__float_as_uint(p8.x) != __float_as_uint(__fdiv_rn(e, 255.0f)));
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        b4 += div_levels<4>(0.0f) != 0.0f || div_levels2<4>(make_float2(0.0f, 0.0f)).x != 0.0f;
+        b8 += div_levels<8>(0.0f) != 0.0f || div_levels2<8>(make_float2(0.0f, 0.0f)).y != 0.0f;
+    }
+    for (uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < 65536u; p += stride) {
+        const float sv = __half2float(__ushort_as_half(uint16_t(p)));
+        const float want = sv > 0.0f ? __frcp_rn(sv) : 0.0f;
+        br += __float_as_uint(rcp_fp16(sv, T)) != __float_as_uint(want);
+    }
+    if (b4) atomicAdd(&bad[0], b4);
+    if (b8) atomicAdd(&bad[1], b8);
+    if (br) atomicAdd(&bad[2], br);
+}
+
+int write_error_flag(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_write_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear && v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_write_error, &zero, sizeof(int));
+    }
+    return v;
 }
 
 }  // namespace kush
@@ -362,4 +995,23 @@ extern "C" int kush_sm100_write(int32_t head_dim, int32_t bits, int32_t page, in
         return set_error(rc, "kush_sm100_write: unsupported head_dim %d / bits %d / page %d / dtype %d", head_dim, bits,
                          page, dtype);
     return rc;
+}
+
+extern "C" int kush_sm100_selfcheck(uint64_t* mismatches) {
+    if (!mismatches) return set_error(KUSH_ERR_ARG, "kush_sm100_selfcheck: null pointer");
+    unsigned long long* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, 3 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(d, 0, 3 * sizeof(unsigned long long));
+    if (e == cudaSuccess) {
+        int sms = 0;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        selfcheck_kernel<<<(sms > 0 ? sms : 1) * 8, 256>>>(d);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (d) cudaFree(d);
+    if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "kush_sm100_selfcheck: %s", cudaGetErrorString(e));
+    return KUSH_OK;
 }
