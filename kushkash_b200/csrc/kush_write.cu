@@ -441,117 +441,156 @@ __device__ __forceinline__ uint32_t unit8(uint32_t a, float2 b, float2 iv) {
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// qparams for one range, scalar (bit-exact as qparams2); returns whether a code of the range can need the clamp
+template <int BITS>
+__device__ __forceinline__ bool qparams1(float mn, float mx, const uint32_t* T, uint16_t& sh, uint16_t& bh, float& b,
+                                         float& inv) {
+    constexpr float HALFF = float(1 << (BITS - 1));
+    constexpr float LO = -HALFF - 0.5f, HI = HALFF - 0.5f;
+    const __half s16 = __float2half_rn(div_levels<BITS>(__fsub_rn(mx, mn)));
+    const float s = __half2float(s16);
+    const __half b16 = __float2half_rn(__fmaf_rn(s, HALFF, mn));       // mn + s * HALF (the product is exact)
+    b = __half2float(b16);
+    inv = rcp_fp16(s, T);
+    sh = __half_as_ushort(s16);
+    bh = __half_as_ushort(b16);
+    const float ylo = __fmul_rn(__fsub_rn(mn, b), inv), yhi = __fmul_rn(__fsub_rn(mx, b), inv);
+    return !(ylo >= LO && yhi < HI);
+}
+
+// Streaming-write geometry.  An item (one page of one kv head) is handled by G = P / 16 warps sharing one ring
+// slot: warp wg of the group encodes V rows [16 wg, 16 wg + 16) and code bytes [wg DCW, (wg + 1) DCW) of the K rows.
 template <int D, int BITS, int P, class IN>
 struct WS {
     using F = Fmt<D, BITS, P>;
+    static constexpr int G = P / 16;                                // warps per item
     static constexpr int ROWB = 2 * D;                              // bytes of an input row
-    static constexpr int STAGE = 2 * P * ROWB;                      // one slot: P K rows, then P V rows
-    static constexpr int NS = 2;                                    // ring slots per warp
-    static constexpr int NW = STAGE <= 8192 ? 4 : 2;                // warps per CTA
+    static constexpr int RSTR = ROWB + 16;                          // slot row stride (skews banks across rows)
+    static constexpr int STAGE = 2 * P * RSTR;                      // one slot: P K rows, then P V rows
+    static constexpr int NS = 2;                                    // ring slots per item stream
+    static constexpr int NW = (4 / G) * NS * STAGE <= 73728 ? 4 : G > 1 ? G : 2;           // warps per CTA
+    static constexpr int NST = NW / G;                              // item streams per CTA
     static constexpr int OFF_BAR = 4096;                            // after the 1024-entry reciprocal table
+    static constexpr int OFF_STOP = OFF_BAR + 64;                   // per stream: a wait gave up
     static constexpr int OFF_STAGE = OFF_BAR + 128;
-    static constexpr int SMEM = OFF_STAGE + NW * NS * STAGE;
-    // V: GL lanes per row (16 values each), RPB rows per pass; passes go in pairs (2 rows per lane)
-    static constexpr int GL = D / 16, RPB = 32 / GL;
-    // K: lane = KC code bytes of a row (int4: KC lo dims + KC hi dims; int8: KC dims), LW lanes per token set,
-    // TS token sets of TPS rows (ranges combined across sets by shuffles)
+    static constexpr int SMEM = OFF_STAGE + NST * NS * STAGE;
+    // V: GL lanes per row, VPL values per lane (int4: VPL/2 lo dims + the matching hi dims), RPP rows per pass
+    static constexpr int GL = D / 64 > 2 ? D / 64 : 2;
+    static constexpr int VPL = D / GL, VW = VPL / 2, RPP = 32 / GL, VPASS = 16 / RPP;
+    // K: lane = KC code bytes of a row (int4: KC lo dims + KC hi dims; int8: KC dims) within the warp's DCW bytes,
+    // LW lanes per token set, TS token sets of TPS rows (ranges combined across sets by shuffles)
     static constexpr int DC = F::DC;
-    static constexpr int KC = DC / 32 > 4 ? DC / 32 : 4;
-    static constexpr int LW = DC / KC, TS = 32 / LW, TPS = P / TS;
+    static constexpr int DCW = DC / G;
+    static constexpr int KC = DCW / 32 > 4 ? DCW / 32 : 4;
+    static constexpr int LW = DCW / KC, TS = 32 / LW, TPS = P / TS;
     static constexpr int NU = KC / 2;                               // 2-byte code units per row per lane
     static constexpr int KWD = BITS == 4 ? KC : KC / 2;             // input words per row per lane
     static constexpr int NPR = BITS == 4 ? 2 * NU : NU;             // channel pairs per lane
     static constexpr bool KREG = TPS * KWD <= 32;                   // keep the K words in registers between passes
-    static_assert((P / RPB) % 2 == 0, "V passes go in pairs");
+    static_assert(P == 16 * G && NW % G == 0 && RPP * VPASS == 16 && (G == 1 || NST <= 2), "geometry");
 };
 
-// 16 V values of row r for lane g: int4: lo dims [8g, 8g + 8) and hi dims D/2 + [8g, 8g + 8) (code bytes
-// [8g, 8g + 8)); int8: dims [16g, 16g + 16) (code bytes [16g, 16g + 16))
-template <int D, int BITS>
-__device__ __forceinline__ void v_words(const uint8_t* row, int g, uint32_t (&w)[8]) {
-    const uint4 a = lds128(row + (BITS == 4 ? 16 * g : 32 * g));
-    const uint4 b = lds128(row + (BITS == 4 ? D + 16 * g : 32 * g + 16));
-    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+// the VW words of V row `row` this lane encodes: int4: lo dims [j VPL/2, (j+1) VPL/2), then the same hi dims;
+// int8: dims [j VPL, (j+1) VPL)
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void v_words(const uint8_t* row, int j, uint32_t (&w)[WS<D, BITS, P, IN>::VW]) {
+    using C = WS<D, BITS, P, IN>;
+    constexpr int NQ = C::VW / 4;                                   // 16-byte loads
+#pragma unroll
+    for (int q = 0; q < NQ; q++) {
+        int off;
+        if constexpr (BITS == 4) off = q < NQ / 2 ? j * C::VPL + 16 * q : D + j * C::VPL + 16 * (q - NQ / 2);
+        else off = 2 * j * C::VPL + 16 * q;
+        const uint4 a = lds128(row + off);
+        w[4 * q] = a.x;
+        w[4 * q + 1] = a.y;
+        w[4 * q + 2] = a.z;
+        w[4 * q + 3] = a.w;
+    }
 }
 
 template <int D, int BITS, int P, class IN, bool CL>
-__device__ __forceinline__ void v_encode(const uint32_t (&w)[8], float bias, float inv, uint8_t* dst, int g) {
+__device__ __forceinline__ void v_encode(const uint32_t (&w)[WS<D, BITS, P, IN>::VW], float bias, float inv,
+                                         uint8_t* dst) {
+    constexpr int VW = WS<D, BITS, P, IN>::VW;
     const float2 b = make_float2(bias, bias), iv = make_float2(inv, inv);
     if constexpr (BITS == 4) {
-        uint32_t o[2];
+        constexpr int NO = VW / 4;                                  // output words (VW/2 units of 2 bytes)
+        uint32_t o[NO];
 #pragma unroll
-        for (int k = 0; k < 2; k++)
-            o[k] = prmt(unit4<IN, CL>(w[2 * k], w[4 + 2 * k], b, iv, b, iv),
-                        unit4<IN, CL>(w[2 * k + 1], w[5 + 2 * k], b, iv, b, iv), 0x5410) ^ 0x88888888u;
-        *reinterpret_cast<uint2*>(dst + 8 * g) = make_uint2(o[0], o[1]);
+        for (int k = 0; k < NO; k++)
+            o[k] = prmt(unit4<IN, CL>(w[2 * k], w[VW / 2 + 2 * k], b, iv, b, iv),
+                        unit4<IN, CL>(w[2 * k + 1], w[VW / 2 + 2 * k + 1], b, iv, b, iv), 0x5410) ^ 0x88888888u;
+#pragma unroll
+        for (int k = 0; k < NO; k += 4) *reinterpret_cast<uint4*>(dst + 4 * k) = make_uint4(o[k], o[k + 1], o[k + 2], o[k + 3]);
     } else {
-        uint32_t o[4];
+        constexpr int NO = VW / 2;
+        uint32_t o[NO];
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            o[k] = prmt(unit8<IN, CL>(w[2 * k], b, iv), unit8<IN, CL>(w[2 * k + 1], b, iv), 0x5410);
-        *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int k = 0; k < NO; k++) o[k] = prmt(unit8<IN, CL>(w[2 * k], b, iv), unit8<IN, CL>(w[2 * k + 1], b, iv), 0x5410);
+#pragma unroll
+        for (int k = 0; k < NO; k += 4) *reinterpret_cast<uint4*>(dst + 4 * k) = make_uint4(o[k], o[k + 1], o[k + 2], o[k + 3]);
     }
 }
 
-// (min, -max) of a row's values in one 16-bit pair word, reduced over the GL lanes of the row
-template <class IN, int GL>
-__device__ __forceinline__ uint32_t row_range(const uint32_t (&w)[8]) {
+// pairwise min / max tree over n words
+template <class IN, int N>
+__device__ __forceinline__ void range_tree(const uint32_t (&w)[N], uint32_t& m, uint32_t& M) {
     using PR = Pair16<IN>;
-    const uint32_t m = PR::min2(PR::min2(PR::min2(w[0], w[1]), PR::min2(w[2], w[3])),
-                                PR::min2(PR::min2(w[4], w[5]), PR::min2(w[6], w[7])));
-    const uint32_t M = PR::max2(PR::max2(PR::max2(w[0], w[1]), PR::max2(w[2], w[3])),
-                                PR::max2(PR::max2(w[4], w[5]), PR::max2(w[6], w[7])));
-    const uint32_t nM = M ^ 0x80008000u;                            // -max: both ranges reduce as one min
-    uint32_t mm = PR::min2(prmt(m, nM, 0x5410), prmt(m, nM, 0x7632));
+    uint32_t a[N / 2], b[N / 2];
 #pragma unroll
-    for (int o = GL / 2; o; o >>= 1) mm = PR::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
-    return mm;
+    for (int i = 0; i < N / 2; i++) {
+        a[i] = PR::min2(w[2 * i], w[2 * i + 1]);
+        b[i] = PR::max2(w[2 * i], w[2 * i + 1]);
+    }
+#pragma unroll
+    for (int s = 1; s < N / 2; s <<= 1)
+#pragma unroll
+        for (int i = 0; i + s < N / 2; i += 2 * s) {
+            a[i] = PR::min2(a[i], a[i + s]);
+            b[i] = PR::max2(b[i], b[i + s]);
+        }
+    m = a[0];
+    M = b[0];
 }
 
-// V rows of a full page from the slot, two rows per lane at a time: rows 2p RPB + lane / GL and (2p + 1) RPB + lane / GL
+// the warp's 16 V rows of a full page from the slot: row 16 wg + pass RPP + lane / GL, lane part j = lane % GL
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, const uint32_t* T, int lane) {
+__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, const uint32_t* T, int lane, int wg) {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
-    const int g = lane % C::GL;
+    const int j = lane % C::GL;
 #pragma unroll 1
-    for (int pp = 0; pp < P / C::RPB / 2; pp++) {
-        const int r0 = 2 * pp * C::RPB + lane / C::GL, r1 = r0 + C::RPB;
-        uint32_t w0[8], w1[8];
-        v_words<D, BITS>(vbuf + r0 * C::ROWB, g, w0);
-        v_words<D, BITS>(vbuf + r1 * C::ROWB, g, w1);
-        const uint32_t mm0 = row_range<IN, C::GL>(w0), mm1 = row_range<IN, C::GL>(w1);
-        uint32_t sh2, bh2;
-        float2 b, inv;
-        const bool need = qparams2<BITS>(make_float2(PR::lo(mm0), PR::lo(mm1)), make_float2(-PR::hi(mm0), -PR::hi(mm1)),
-                                         T, sh2, bh2, b, inv);
-        if (g == 0) {
-            uint16_t* vs = reinterpret_cast<uint16_t*>(rec + F::OFF_VS);
-            uint16_t* vb = reinterpret_cast<uint16_t*>(rec + F::OFF_VB);
-            vs[r0] = uint16_t(sh2);
-            vs[r1] = uint16_t(sh2 >> 16);
-            vb[r0] = uint16_t(bh2);
-            vb[r1] = uint16_t(bh2 >> 16);
+    for (int pass = 0; pass < C::VPASS; pass++) {
+        const int r = 16 * wg + pass * C::RPP + lane / C::GL;
+        uint32_t w[C::VW];
+        v_words<D, BITS, P, IN>(vbuf + r * C::RSTR, j, w);
+        uint32_t m, M;
+        range_tree<IN, C::VW>(w, m, M);
+        const uint32_t nM = M ^ 0x80008000u;                        // -max: both ranges reduce as one min
+        uint32_t mm = PR::min2(prmt(m, nM, 0x5410), prmt(m, nM, 0x7632));       // (min, -max)
+#pragma unroll
+        for (int o = C::GL / 2; o; o >>= 1) mm = PR::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        uint16_t sh, bh;
+        float b, inv;
+        const bool need = qparams1<BITS>(PR::lo(mm), -PR::hi(mm), T, sh, bh, b, inv);
+        if (j == 0) {
+            reinterpret_cast<uint16_t*>(rec + F::OFF_VS)[r] = sh;
+            reinterpret_cast<uint16_t*>(rec + F::OFF_VB)[r] = bh;
         }
-        uint8_t* q = rec + F::OFF_VQ;
-        if (__any_sync(0xffffffffu, need)) {
-            v_encode<D, BITS, P, IN, true>(w0, b.x, inv.x, q + r0 * F::DC, g);
-            v_encode<D, BITS, P, IN, true>(w1, b.y, inv.y, q + r1 * F::DC, g);
-        } else {
-            v_encode<D, BITS, P, IN, false>(w0, b.x, inv.x, q + r0 * F::DC, g);
-            v_encode<D, BITS, P, IN, false>(w1, b.y, inv.y, q + r1 * F::DC, g);
-        }
+        uint8_t* dst = rec + F::OFF_VQ + r * F::DC + j * (F::DC / C::GL);
+        if (__any_sync(0xffffffffu, need)) v_encode<D, BITS, P, IN, true>(w, b, inv, dst);
+        else v_encode<D, BITS, P, IN, false>(w, b, inv, dst);
     }
 }
 
-// this lane's K input words of row t: int4: KC/2 words of lo dims [c KC, c KC + KC), then the same of hi dims;
-// int8: KC/2 words of dims [c KC, c KC + KC)
+// this lane's K input words of row t: int4: KC/2 words of lo dims [e0, e0 + KC), then the same of hi dims;
+// int8: KC/2 words of dims [e0, e0 + KC); e0 = the lane's first code byte
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_k_words(const uint8_t* kbuf, int t, int c, uint32_t (&w)[WS<D, BITS, P, IN>::KWD]) {
+__device__ __forceinline__ void ws_k_words(const uint8_t* kbuf, int t, int e0, uint32_t (&w)[WS<D, BITS, P, IN>::KWD]) {
     using C = WS<D, BITS, P, IN>;
-    const uint8_t* row = kbuf + t * C::ROWB + 2 * c * C::KC;
+    const uint8_t* row = kbuf + t * C::RSTR + 2 * e0;
     if constexpr (C::KC == 4) {
         const uint2 a = *reinterpret_cast<const uint2*>(row);
         w[0] = a.x;
@@ -590,24 +629,26 @@ __device__ __forceinline__ void k_encode(const uint32_t (&w)[WS<D, BITS, P, IN>:
     }
 }
 
-// K of a full page from the slot: per-channel ranges over the P rows, then the codes
+// the warp's K code bytes [wg DCW, (wg + 1) DCW) of a full page from the slot: per-channel ranges over the P rows,
+// then the codes
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, const uint32_t* T, int lane) {
+__device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, const uint32_t* T, int lane, int wg) {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
     constexpr int KWD = C::KWD, NU = C::NU, NPR = C::NPR;
     constexpr int TR = C::KREG ? C::TPS : 1;                         // rows whose words stay in registers
     const int c = lane % C::LW, t0 = (lane / C::LW) * C::TPS;
+    const int e0 = wg * C::DCW + c * C::KC;                          // first code byte of the lane
     uint32_t kw[TR][KWD];
     uint32_t mn[KWD], mx[KWD];
-    ws_k_words<D, BITS, P, IN>(kbuf, t0, c, kw[0]);
+    ws_k_words<D, BITS, P, IN>(kbuf, t0, e0, kw[0]);
 #pragma unroll
     for (int i = 0; i < KWD; i++) mn[i] = mx[i] = kw[0][i];
 #pragma unroll
     for (int t = 1; t < C::TPS; t++) {
         uint32_t w[KWD];
-        ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, c, w);
+        ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, e0, w);
 #pragma unroll
         for (int i = 0; i < KWD; i++) {
             if constexpr (C::KREG) kw[t < TR ? t : 0][i] = w[i];
@@ -622,7 +663,7 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, con
             mn[i] = PR::min2(mn[i], __shfl_xor_sync(0xffffffffu, mn[i], o));
             mx[i] = PR::max2(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
         }
-    // channel pairs: int4 pair 2u + p = (lo dim 2u + p, hi dim 2u + p) of the lane; int8 pair u = (dim 2u, 2u + 1)
+    // channel pairs: int4 pair 2u + p = (lo dim e0 + 2u + p, hi dim e0 + 2u + p); int8 pair u = (dims e0 + 2u, + 1)
     float2 b[NPR], iv[NPR];
     uint32_t sh[NPR], bh[NPR];
     bool need = false;
@@ -648,19 +689,19 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, con
             const uint2 s_hi = make_uint2(prmt(sh[0], sh[1], 0x7632), prmt(sh[2], sh[3], 0x7632));
             const uint2 b_lo = make_uint2(prmt(bh[0], bh[1], 0x5410), prmt(bh[2], bh[3], 0x5410));
             const uint2 b_hi = make_uint2(prmt(bh[0], bh[1], 0x7632), prmt(bh[2], bh[3], 0x7632));
-            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * c * C::KC) = s_lo;
-            *reinterpret_cast<uint2*>(rec + F::OFF_KS + D + 2 * c * C::KC) = s_hi;
-            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * c * C::KC) = b_lo;
-            *reinterpret_cast<uint2*>(rec + F::OFF_KB + D + 2 * c * C::KC) = b_hi;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * e0) = s_lo;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KS + D + 2 * e0) = s_hi;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * e0) = b_lo;
+            *reinterpret_cast<uint2*>(rec + F::OFF_KB + D + 2 * e0) = b_hi;
         } else if constexpr (NU == 2) {
-            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * c * C::KC) = make_uint2(sh[0], sh[1]);
-            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * c * C::KC) = make_uint2(bh[0], bh[1]);
+            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * e0) = make_uint2(sh[0], sh[1]);
+            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * e0) = make_uint2(bh[0], bh[1]);
         } else {
-            *reinterpret_cast<uint4*>(rec + F::OFF_KS + 2 * c * C::KC) = make_uint4(sh[0], sh[1], sh[2], sh[3]);
-            *reinterpret_cast<uint4*>(rec + F::OFF_KB + 2 * c * C::KC) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
+            *reinterpret_cast<uint4*>(rec + F::OFF_KS + 2 * e0) = make_uint4(sh[0], sh[1], sh[2], sh[3]);
+            *reinterpret_cast<uint4*>(rec + F::OFF_KB + 2 * e0) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
         }
     }
-    uint8_t* dst = rec + t0 * F::DC + c * C::KC;
+    uint8_t* dst = rec + t0 * F::DC + e0;
     const bool cl = __any_sync(0xffffffffu, need);
 #pragma unroll
     for (int t = 0; t < C::TPS; t++) {
@@ -669,7 +710,7 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, con
 #pragma unroll
             for (int i = 0; i < KWD; i++) w[i] = kw[t][i];
         } else {
-            ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, c, w);
+            ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, e0, w);
         }
         if (cl) k_encode<D, BITS, P, IN, true>(w, b, iv, dst + t * F::DC);
         else k_encode<D, BITS, P, IN, false>(w, b, iv, dst + t * F::DC);
@@ -680,6 +721,20 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, con
 struct WMeta {
     int row0, hf, blk, s, pg, q0, ctx, total;
 };
+
+// the G warps of an item stream: one warp syncs itself, a pair of warps takes named barrier 1 + stream (immediate
+// ids: the kernel reserves only the barriers it names)
+template <int G>
+__device__ __forceinline__ void group_sync(int stream) {
+    static_assert(G == 1 || G == 2, "one or two warps per item");
+    if constexpr (G == 1) {
+        __syncwarp();
+    } else if (stream == 0) {
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+    } else {
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+    }
+}
 
 template <int D, int BITS, int P, class IN>
 __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
@@ -695,17 +750,20 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
     uint32_t* T = reinterpret_cast<uint32_t*>(wsm);
     uint64_t* bars = reinterpret_cast<uint64_t*>(wsm + C::OFF_BAR);
     const int lane = threadIdx.x % WARP, w = threadIdx.x / WARP;
+    const int st = w / C::G, wg = w % C::G;                          // item stream of the CTA, warp within it
     for (int i = threadIdx.x; i < 1024; i += blockDim.x)
         T[i] = __float_as_uint(__frcp_rn(1.0f + float(i) * (1.0f / 1024.0f)));
-    if (threadIdx.x < C::NW * C::NS) mbar_init(&bars[threadIdx.x], 1);
+    volatile int* stop = reinterpret_cast<volatile int*>(wsm + C::OFF_STOP);
+    if (threadIdx.x < C::NST * C::NS) mbar_init(&bars[threadIdx.x], 1);
+    if (threadIdx.x < C::NST) stop[threadIdx.x] = 0;
     fence_mbar_init();
     __syncthreads();
 
-    uint8_t* slots = wsm + C::OFF_STAGE + w * C::NS * C::STAGE;
-    const uint32_t bar0 = smem_u32(&bars[w * C::NS]);
+    uint8_t* slots = wsm + C::OFF_STAGE + st * C::NS * C::STAGE;
+    const uint32_t bar0 = smem_u32(&bars[st * C::NS]);
     const int64_t n_items = int64_t(n_jobs) * H;
-    const int64_t TW = int64_t(gridDim.x) * C::NW;
-    const int64_t first = int64_t(blockIdx.x) * C::NW + w;
+    const int64_t TW = int64_t(gridDim.x) * C::NST;
+    const int64_t first = int64_t(blockIdx.x) * C::NST + st;
     const int n_local = first < n_items ? int((n_items - first + TW - 1) / TW) : 0;
 
     auto load_meta = [&](int batch) {
@@ -728,12 +786,12 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
     };
     WMeta cur = load_meta(0), nxt = load_meta(1);
 #define KUSH_META(field, use_b, l) __shfl_sync(0xffffffffu, (use_b) ? nxt.field : cur.field, (l))
-    // bring the rows of full item i (first input row row0, kv head h) into slot i % NS
+    // warp 0 of the stream brings the rows of full item i (first input row row0, kv head h) into slot i % NS
     auto issue = [&](int i, int row0, int h) {
         const uint32_t bar = bar0 + 8u * uint32_t(i % C::NS);
         const uint32_t dst = smem_u32(slots + (i % C::NS) * C::STAGE);
         if (lane == 0)
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(uint32_t(C::STAGE))
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(uint32_t(2 * P * C::ROWB))
                          : "memory");
         __syncwarp();
 #pragma unroll
@@ -741,12 +799,13 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
             const IN* src = r < P ? k_new + (int64_t(row0) + r) * k_stride + int64_t(h) * D
                                   : v_new + (int64_t(row0) + r - P) * v_stride + int64_t(h) * D;
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                             dst + uint32_t(r * C::ROWB)),
+                             dst + uint32_t(r * C::RSTR)),
                          "l"(src), "r"(uint32_t(C::ROWB)), "r"(bar)
                          : "memory");
         }
     };
-    // every other item: the warp-level per-token path (mode 0 / 1 / 2 as write_kernel), slot i % NS as scratch
+    // every other item: the warp-level per-token path (mode 0 / 1 / 2 as write_kernel) by warp 0 of the stream,
+    // slot i % NS as scratch
     auto general = [&](int i, int l, int h, int blk) {
         const int64_t ps = int64_t(KUSH_META(pg, false, l)) * P, ctx = KUSH_META(ctx, false, l);
         const int64_t total = KUSH_META(total, false, l), q0 = KUSH_META(q0, false, l);
@@ -783,9 +842,11 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the slot may next be filled by a bulk copy
     };
 
-    for (int i = 0; i < C::NS - 1 && i < n_local; i++) {
-        const int hf = KUSH_META(hf, false, i);
-        if (hf & FULL) issue(i, KUSH_META(row0, false, i), hf & (FULL - 1));
+    if (wg == 0) {
+        for (int i = 0; i < C::NS - 1 && i < n_local; i++) {
+            const int hf = KUSH_META(hf, false, i);
+            if (hf & FULL) issue(i, KUSH_META(row0, false, i), hf & (FULL - 1));
+        }
     }
     uint32_t phase = 0;
     for (int i = 0; i < n_local; i++) {
@@ -794,7 +855,7 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
             nxt = load_meta(i / WARP + 1);
         }
         const int ia = i + C::NS - 1;                                // the item whose rows start now
-        if (ia < n_local) {
+        if (wg == 0 && ia < n_local) {
             const bool nb = ia / WARP != i / WARP;
             const int hfa = KUSH_META(hf, nb, ia % WARP);
             if (hfa & FULL) issue(ia, KUSH_META(row0, nb, ia % WARP), hfa & (FULL - 1));
@@ -802,26 +863,35 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
         const int l = i % WARP;
         const int hf = KUSH_META(hf, false, l), blk = KUSH_META(blk, false, l);
         const int h = hf & (FULL - 1), slot = i % C::NS;
+        bool ok = true;
         if (hf & FULL) {
-            if (!__all_sync(0xffffffffu, mbar_wait_u32(bar0 + 8u * slot, (phase >> slot) & 1u))) {
-                // a copy never completed: record it, wait (bounded) for this warp's other copies, stop
-                if (lane == 0) atomicExch(&g_write_error, 1);
+            ok = __all_sync(0xffffffffu, mbar_wait_u32(bar0 + 8u * slot, (phase >> slot) & 1u));
+            if (ok) {
+                phase ^= 1u << slot;
+                const uint8_t* kbuf = slots + slot * C::STAGE;
+                uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
+                ws_v_rows<D, BITS, P, IN>(kbuf + P * C::RSTR, rec, T, lane, wg);
+                ws_k_page<D, BITS, P, IN>(kbuf, rec, T, lane, wg);
+            }
+        } else if (wg == 0) {
+            general(i, l, h, blk);
+        }
+        if (!ok && lane == 0) {
+            atomicExch(&g_write_error, 1);
+            stop[st] = 1;
+        }
+        group_sync<C::G>(st);                                        // the slot is free for the next issue
+        if (stop[st]) {
+            // a copy never completed: warp 0 waits (bounded) for the stream's other copies, then the stream stops
+            if (wg == 0) {
                 for (int k = i + 1; k < i + C::NS && k < n_local; k++) {
                     const int sk = k % C::NS;
                     if (KUSH_META(hf, k / WARP != i / WARP, k % WARP) & FULL)
-                        mbar_wait_u32(bar0 + 8u * sk, (phase >> sk) & 1u);
+                        mbar_wait_u32(bar0 + 8u * sk, ((phase >> sk) & 1u));
                 }
-                return;
             }
-            phase ^= 1u << slot;
-            const uint8_t* kbuf = slots + slot * C::STAGE;
-            uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
-            ws_v_rows<D, BITS, P, IN>(kbuf + P * C::ROWB, rec, T, lane);
-            ws_k_page<D, BITS, P, IN>(kbuf, rec, T, lane);
-        } else {
-            general(i, l, h, blk);
+            return;
         }
-        __syncwarp();
     }
 #undef KUSH_META
 }
@@ -860,7 +930,7 @@ int launch_write_stream(const void* k_new, const void* v_new, int64_t k_stride, 
         slots = per_sm * sms;
         resident[di].store(slots, std::memory_order_relaxed);
     }
-    const int64_t want = (int64_t(n_jobs) * hkv + C::NW - 1) / C::NW;
+    const int64_t want = (int64_t(n_jobs) * hkv + C::NST - 1) / C::NST;
     const int grid = int(want < slots ? want : slots);
     kern<<<grid, C::NW * WARP, C::SMEM, stream>>>(
         static_cast<const IN*>(k_new), static_cast<const IN*>(v_new), k_stride, v_stride, qsl, seq_lens, tail_idx,
