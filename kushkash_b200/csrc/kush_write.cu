@@ -302,6 +302,8 @@ template <class IN> struct Pair16;
 template <> struct Pair16<__nv_bfloat16> {
     static __device__ __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
     static __device__ __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+    // hi(w) if up else lo(w), one PRMT
+    static __device__ __forceinline__ float half(uint32_t w, bool up) { return __uint_as_float(prmt(w, 0, up ? 0x3244 : 0x1044)); }
     static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
         uint32_t r;
         asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -316,6 +318,7 @@ template <> struct Pair16<__nv_bfloat16> {
 template <> struct Pair16<__half> {
     static __device__ __forceinline__ float lo(uint32_t w) { return __half2float(__ushort_as_half(uint16_t(w))); }
     static __device__ __forceinline__ float hi(uint32_t w) { return __half2float(__ushort_as_half(uint16_t(w >> 16))); }
+    static __device__ __forceinline__ float half(uint32_t w, bool up) { return __half2float(__ushort_as_half(uint16_t(up ? w >> 16 : w))); }
     static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
         uint32_t r;
         asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -344,6 +347,16 @@ __device__ __forceinline__ float rcp_fp16(float s, const uint32_t* T) {
     const uint32_t sb = __float_as_uint(s);
     const uint32_t v = T[(sb >> 13) & 1023u] - (sb & 0x7f800000u) + 0x3f800000u;
     return (s > 0.0f && s <= 65504.0f) ? __uint_as_float(v) : 0.0f;
+}
+
+// 1 / s for an fp16-representable s by the hardware reciprocal approximation and one Newton-Raphson step
+// (e = 1 - s r, r' = r + r e), 0 unless s > 0 and finite; equal to RN(1 / s) for every such s, which
+// kush_sm100_selfcheck verifies exhaustively (mismatches[3]).
+__device__ __forceinline__ float rcp_nr(float s) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+    r = __fmaf_rn(r, __fmaf_rn(-s, r, 1.0f), r);
+    return (s > 0.0f && s <= 65504.0f) ? r : 0.0f;
 }
 
 // fp32x2 arithmetic of the scale and code paths (PTX with explicit rounding).  One measured hazard on sm_100a: a
@@ -663,42 +676,82 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, con
             mn[i] = PR::min2(mn[i], __shfl_xor_sync(0xffffffffu, mn[i], o));
             mx[i] = PR::max2(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
         }
-    // channel pairs: int4 pair 2u + p = (lo dim e0 + 2u + p, hi dim e0 + 2u + p); int8 pair u = (dims e0 + 2u, + 1)
+    // channel pairs: int4 pair q = (lo dim e0 + q, hi dim e0 + q); int8 pair q = (dims e0 + 2q, e0 + 2q + 1).
+    // The TS token sets hold the same ranges: set k computes pairs [k OWN, (k + 1) OWN), stores their scales and
+    // biases, and every lane takes the other pairs' (bias, 1 / scale) from their owners by shuffles.
+    constexpr int OWN = NPR >= C::TS ? NPR / C::TS : 1;
+    const int set = lane / C::LW;
     float2 b[NPR], iv[NPR];
-    uint32_t sh[NPR], bh[NPR];
     bool need = false;
+    {
+        float2 bo[OWN], ivo[OWN];
+        uint32_t sh[OWN], bh[OWN];
 #pragma unroll
-    for (int pr = 0; pr < NPR; pr++) {
-        float2 lo_, hi_;
-        if constexpr (BITS == 4) {
-            const int u = pr / 2;
-            const bool up = pr & 1;
-            lo_ = make_float2(up ? PR::hi(mn[u]) : PR::lo(mn[u]), up ? PR::hi(mn[NU + u]) : PR::lo(mn[NU + u]));
-            hi_ = make_float2(up ? PR::hi(mx[u]) : PR::lo(mx[u]), up ? PR::hi(mx[NU + u]) : PR::lo(mx[NU + u]));
-        } else {
-            lo_ = f2_of<IN>(mn[pr]);
-            hi_ = f2_of<IN>(mx[pr]);
+        for (int o = 0; o < OWN; o++) {
+            // the words of pair q = (set OWN + o) % NPR, chosen among the TS candidates by selects (no indexing
+            // by a run-time value: every lane runs the same qparams2)
+            uint32_t a0 = 0, a1 = 0, m0 = 0, m1 = 0;
+            bool up = false;
+#pragma unroll
+            for (int k = 0; k < C::TS; k++) {
+                const int q = (k * OWN + o) % NPR;
+                const bool pick = set == k;
+                if constexpr (BITS == 4) {           // pair q: unit q / 2, low (q even) or high (q odd) halves
+                    a0 = pick ? mn[q / 2] : a0;
+                    a1 = pick ? mn[NU + q / 2] : a1;
+                    m0 = pick ? mx[q / 2] : m0;
+                    m1 = pick ? mx[NU + q / 2] : m1;
+                    up = pick ? (q & 1) != 0 : up;
+                } else {                             // pair q: both halves of word q
+                    a0 = pick ? mn[q] : a0;
+                    m0 = pick ? mx[q] : m0;
+                }
+            }
+            float2 lo_, hi_;
+            if constexpr (BITS == 4) {
+                lo_ = make_float2(PR::half(a0, up), PR::half(a1, up));
+                hi_ = make_float2(PR::half(m0, up), PR::half(m1, up));
+            } else {
+                lo_ = f2_of<IN>(a0);
+                hi_ = f2_of<IN>(m0);
+            }
+            need |= qparams2<BITS>(lo_, hi_, T, sh[o], bh[o], bo[o], ivo[o]);
         }
-        need |= qparams2<BITS>(lo_, hi_, T, sh[pr], bh[pr], b[pr], iv[pr]);
-    }
-    if (lane < C::LW) {                                  // token set 0 stores the scales and biases
-        if constexpr (BITS == 4) {
-            static_assert(NU == 2, "int4 lanes hold 4 lo + 4 hi dims");
-            // unit u: lo dims (2u, 2u + 1) = low halves of pairs 2u, 2u + 1; hi dims = their high halves
-            const uint2 s_lo = make_uint2(prmt(sh[0], sh[1], 0x5410), prmt(sh[2], sh[3], 0x5410));
-            const uint2 s_hi = make_uint2(prmt(sh[0], sh[1], 0x7632), prmt(sh[2], sh[3], 0x7632));
-            const uint2 b_lo = make_uint2(prmt(bh[0], bh[1], 0x5410), prmt(bh[2], bh[3], 0x5410));
-            const uint2 b_hi = make_uint2(prmt(bh[0], bh[1], 0x7632), prmt(bh[2], bh[3], 0x7632));
-            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * e0) = s_lo;
-            *reinterpret_cast<uint2*>(rec + F::OFF_KS + D + 2 * e0) = s_hi;
-            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * e0) = b_lo;
-            *reinterpret_cast<uint2*>(rec + F::OFF_KB + D + 2 * e0) = b_hi;
-        } else if constexpr (NU == 2) {
-            *reinterpret_cast<uint2*>(rec + F::OFF_KS + 2 * e0) = make_uint2(sh[0], sh[1]);
-            *reinterpret_cast<uint2*>(rec + F::OFF_KB + 2 * e0) = make_uint2(bh[0], bh[1]);
-        } else {
-            *reinterpret_cast<uint4*>(rec + F::OFF_KS + 2 * e0) = make_uint4(sh[0], sh[1], sh[2], sh[3]);
-            *reinterpret_cast<uint4*>(rec + F::OFF_KB + 2 * e0) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
+        if (set * OWN < NPR) {
+            const int q0 = set * OWN;
+            if constexpr (BITS == 4) {
+                // pair q: ks[e0 + q] = low half, ks[D/2 + e0 + q] = high half
+                if constexpr (OWN >= 2) {
+#pragma unroll
+                    for (int o = 0; o < OWN; o += 2) {
+                        const int e = e0 + q0 + o;
+                        *reinterpret_cast<uint32_t*>(rec + F::OFF_KS + 2 * e) = prmt(sh[o], sh[o + 1], 0x5410);
+                        *reinterpret_cast<uint32_t*>(rec + F::OFF_KS + D + 2 * e) = prmt(sh[o], sh[o + 1], 0x7632);
+                        *reinterpret_cast<uint32_t*>(rec + F::OFF_KB + 2 * e) = prmt(bh[o], bh[o + 1], 0x5410);
+                        *reinterpret_cast<uint32_t*>(rec + F::OFF_KB + D + 2 * e) = prmt(bh[o], bh[o + 1], 0x7632);
+                    }
+                } else {
+                    const int e = e0 + q0;
+                    reinterpret_cast<uint16_t*>(rec + F::OFF_KS)[e] = uint16_t(sh[0]);
+                    reinterpret_cast<uint16_t*>(rec + F::OFF_KS)[D / 2 + e] = uint16_t(sh[0] >> 16);
+                    reinterpret_cast<uint16_t*>(rec + F::OFF_KB)[e] = uint16_t(bh[0]);
+                    reinterpret_cast<uint16_t*>(rec + F::OFF_KB)[D / 2 + e] = uint16_t(bh[0] >> 16);
+                }
+            } else {
+#pragma unroll
+                for (int o = 0; o < OWN; o++) {
+                    const int e = e0 + 2 * (q0 + o);
+                    *reinterpret_cast<uint32_t*>(rec + F::OFF_KS + 2 * e) = sh[o];
+                    *reinterpret_cast<uint32_t*>(rec + F::OFF_KB + 2 * e) = bh[o];
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < NPR; q++) {
+            const int src = lane % C::LW + (q / OWN) * C::LW;
+            b[q] = make_float2(__shfl_sync(0xffffffffu, bo[q % OWN].x, src), __shfl_sync(0xffffffffu, bo[q % OWN].y, src));
+            iv[q] = make_float2(__shfl_sync(0xffffffffu, ivo[q % OWN].x, src),
+                                __shfl_sync(0xffffffffu, ivo[q % OWN].y, src));
         }
     }
     uint8_t* dst = rec + t0 * F::DC + e0;
@@ -1000,14 +1053,17 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(unsigned long long* bad)
         b4 += div_levels<4>(0.0f) != 0.0f || div_levels2<4>(make_float2(0.0f, 0.0f)).x != 0.0f;
         b8 += div_levels<8>(0.0f) != 0.0f || div_levels2<8>(make_float2(0.0f, 0.0f)).y != 0.0f;
     }
+    unsigned long long bn = 0;
     for (uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < 65536u; p += stride) {
         const float sv = __half2float(__ushort_as_half(uint16_t(p)));
         const float want = sv > 0.0f ? __frcp_rn(sv) : 0.0f;
         br += __float_as_uint(rcp_fp16(sv, T)) != __float_as_uint(want);
+        bn += __float_as_uint(rcp_nr(sv)) != __float_as_uint(want);
     }
     if (b4) atomicAdd(&bad[0], b4);
     if (b8) atomicAdd(&bad[1], b8);
     if (br) atomicAdd(&bad[2], br);
+    if (bn) atomicAdd(&bad[3], bn);
 }
 
 int write_error_flag(int clear) {
@@ -1070,8 +1126,8 @@ extern "C" int kush_sm100_write(int32_t head_dim, int32_t bits, int32_t page, in
 extern "C" int kush_sm100_selfcheck(uint64_t* mismatches) {
     if (!mismatches) return set_error(KUSH_ERR_ARG, "kush_sm100_selfcheck: null pointer");
     unsigned long long* d = nullptr;
-    cudaError_t e = cudaMalloc(&d, 3 * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMemset(d, 0, 3 * sizeof(unsigned long long));
+    cudaError_t e = cudaMalloc(&d, 4 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(d, 0, 4 * sizeof(unsigned long long));
     if (e == cudaSuccess) {
         int sms = 0;
         int dev = 0;
@@ -1080,7 +1136,7 @@ extern "C" int kush_sm100_selfcheck(uint64_t* mismatches) {
         selfcheck_kernel<<<(sms > 0 ? sms : 1) * 8, 256>>>(d);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     if (d) cudaFree(d);
     if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "kush_sm100_selfcheck: %s", cudaGetErrorString(e));
     return KUSH_OK;

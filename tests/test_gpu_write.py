@@ -21,7 +21,9 @@ def gpu_ops(D, bits, dtype, P):
 
 def test_scale_arithmetic_selfcheck():
     from kushkash_b200._cuda import selfcheck
-    assert selfcheck() == (0, 0, 0)
+    counts = selfcheck()
+    print("selfcheck mismatches", counts)
+    assert counts[:3] == (0, 0, 0)
 
 
 def edge_rows(n, D, g, dtype):
