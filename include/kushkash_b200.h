@@ -116,10 +116,10 @@ int kush_sm100_device_error(int32_t clear);
 
 /* Exhaustive self-check of the bulk write's scale arithmetic on the current device: mismatches[0] / [1] = fp32
  * values d in [2^-100, 2^100] for which the write's d / 15 / d / 255 (Markstein's correction step, scalar and
- * fp32x2 forms) differs from the IEEE quotient, mismatches[2] / [3] = fp16 scales whose reciprocal (table of
- * RN(1 / (1 + i / 1024)) scaled by a power of two / hardware approximation plus one Newton step) differs from the
- * IEEE reciprocal.  All four are 0 on a correct build.  Synchronous; allocates 32 bytes of device memory.  No
- * counterpart in the reference (a diagnostic of this implementation's arithmetic). */
+ * fp32x2 forms) differs from the IEEE quotient, mismatches[2] = fp16 scales whose reciprocal (hardware
+ * approximation plus one Newton step) differs from the IEEE reciprocal.  All three are 0 on a correct build.
+ * Synchronous; allocates 24 bytes of device memory.  No counterpart in the reference (a diagnostic of this
+ * implementation's arithmetic). */
 int kush_sm100_selfcheck(uint64_t *mismatches);
 
 /* Canonical Walsh-Hadamard rotation of `rows` rows of head_dim values: y[r] = fwht(x[r]) (row strides in

@@ -294,8 +294,9 @@ __global__ void __launch_bounds__(D) write_kernel(const IN* __restrict__ k_new, 
 //
 // Scale arithmetic, bit-exact with qparams: (mx - mn) / (2^BITS - 1) by Markstein's correction step (q0 = d * R,
 // r = fma(-q0, L, d), q = fma(r, R, q0) with R = RN(1 / L): the correctly rounded quotient when q0 is within an ulp
-// and nothing under- or overflows; other d take the IEEE divide), and 1 / s from a table of RN(1 / (1 + i / 1024)):
-// every fp16 value s is m * 2^e with a 10-bit fraction, so RN(1 / s) = RN(1 / m) * 2^-e exactly.
+// and nothing under- or overflows; other d take the IEEE divide), and 1 / s for the fp16 scale s by the hardware
+// reciprocal approximation plus one Newton step.  kush_sm100_selfcheck verifies both exhaustively against IEEE
+// division: every fp32 d of the Markstein range, every fp16 s.
 __device__ int g_write_error = 0;              // set when a bounded wait of the streaming write gave up
 
 template <class IN> struct Pair16;
@@ -342,16 +343,9 @@ __device__ __forceinline__ float div_levels(float d) {
     return q;
 }
 
-// RN(1 / s) for an fp16-representable s (s > 0 and finite), else 0 -- qparams' `s > 0 ? 1 / s : 0`
-__device__ __forceinline__ float rcp_fp16(float s, const uint32_t* T) {
-    const uint32_t sb = __float_as_uint(s);
-    const uint32_t v = T[(sb >> 13) & 1023u] - (sb & 0x7f800000u) + 0x3f800000u;
-    return (s > 0.0f && s <= 65504.0f) ? __uint_as_float(v) : 0.0f;
-}
-
-// 1 / s for an fp16-representable s by the hardware reciprocal approximation and one Newton-Raphson step
-// (e = 1 - s r, r' = r + r e), 0 unless s > 0 and finite; equal to RN(1 / s) for every such s, which
-// kush_sm100_selfcheck verifies exhaustively (mismatches[3]).
+// qparams' `s > 0 ? 1 / s : 0` for an fp16-representable s: the hardware reciprocal approximation and one
+// Newton-Raphson step (e = 1 - s r, r' = r + r e), 0 unless s > 0 and finite; RN(1 / s) for every fp16 s (checked
+// exhaustively by kush_sm100_selfcheck).
 __device__ __forceinline__ float rcp_nr(float s) {
     float r;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
@@ -399,7 +393,7 @@ __device__ __forceinline__ float2 div_levels2(float2 d) {
 // as half2 bits and whether any value of either range can need qcode's clamp: the code of a value is monotone in
 // it, so when the codes of both ends (mn, mx) are inside the code range, every code is.
 template <int BITS>
-__device__ __forceinline__ bool qparams2(float2 mn, float2 mx, const uint32_t* T, uint32_t& sh2, uint32_t& bh2,
+__device__ __forceinline__ bool qparams2(float2 mn, float2 mx, uint32_t& sh2, uint32_t& bh2,
                                          float2& b, float2& inv) {
     constexpr float HALFF = float(1 << (BITS - 1));
     constexpr float LO = -HALFF - 0.5f, HI = HALFF - 0.5f;          // round(y) in range <=> LO <= y < HI
@@ -411,7 +405,7 @@ __device__ __forceinline__ bool qparams2(float2 mn, float2 mx, const uint32_t* T
     const float2 bp = fma2_rn(s, make_float2(HALFF, HALFF), mn);   // mn + s * HALF (the product is exact)
     const __half2 b16 = __floats2half2_rn(bp.x, bp.y);
     b = __half22float2(b16);
-    inv = make_float2(rcp_fp16(s.x, T), rcp_fp16(s.y, T));
+    inv = make_float2(rcp_nr(s.x), rcp_nr(s.y));
     sh2 = *reinterpret_cast<const uint32_t*>(&s16);
     bh2 = *reinterpret_cast<const uint32_t*>(&b16);
     const float2 ylo = mul2_rn(fma2_rn(b, m1, mn), inv), yhi = mul2_rn(fma2_rn(b, m1, mx), inv);
@@ -456,7 +450,7 @@ __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_
 
 // qparams for one range, scalar (bit-exact as qparams2); returns whether a code of the range can need the clamp
 template <int BITS>
-__device__ __forceinline__ bool qparams1(float mn, float mx, const uint32_t* T, uint16_t& sh, uint16_t& bh, float& b,
+__device__ __forceinline__ bool qparams1(float mn, float mx, uint16_t& sh, uint16_t& bh, float& b,
                                          float& inv) {
     constexpr float HALFF = float(1 << (BITS - 1));
     constexpr float LO = -HALFF - 0.5f, HI = HALFF - 0.5f;
@@ -464,7 +458,7 @@ __device__ __forceinline__ bool qparams1(float mn, float mx, const uint32_t* T, 
     const float s = __half2float(s16);
     const __half b16 = __float2half_rn(__fmaf_rn(s, HALFF, mn));       // mn + s * HALF (the product is exact)
     b = __half2float(b16);
-    inv = rcp_fp16(s, T);
+    inv = rcp_nr(s);
     sh = __half_as_ushort(s16);
     bh = __half_as_ushort(b16);
     const float ylo = __fmul_rn(__fsub_rn(mn, b), inv), yhi = __fmul_rn(__fsub_rn(mx, b), inv);
@@ -483,9 +477,9 @@ struct WS {
     static constexpr int NS = 2;                                    // ring slots per item stream
     static constexpr int NW = (4 / G) * NS * STAGE <= 73728 ? 4 : G > 1 ? G : 2;           // warps per CTA
     static constexpr int NST = NW / G;                              // item streams per CTA
-    static constexpr int OFF_BAR = 4096;                            // after the 1024-entry reciprocal table
-    static constexpr int OFF_STOP = OFF_BAR + 64;                   // per stream: a wait gave up
-    static constexpr int OFF_STAGE = OFF_BAR + 128;
+    static constexpr int OFF_BAR = 0;                               // NST * NS mbarriers
+    static constexpr int OFF_STOP = 64;                             // per stream: a wait gave up
+    static constexpr int OFF_STAGE = 128;
     static constexpr int SMEM = OFF_STAGE + NST * NS * STAGE;
     // V: GL lanes per row, VPL values per lane (int4: VPL/2 lo dims + the matching hi dims), RPP rows per pass
     static constexpr int GL = D / 64 > 2 ? D / 64 : 2;
@@ -569,7 +563,7 @@ __device__ __forceinline__ void range_tree(const uint32_t (&w)[N], uint32_t& m, 
 
 // the warp's 16 V rows of a full page from the slot: row 16 wg + pass RPP + lane / GL, lane part j = lane % GL
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, const uint32_t* T, int lane, int wg) {
+__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, int lane, int wg) {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
@@ -587,7 +581,7 @@ __device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, con
         for (int o = C::GL / 2; o; o >>= 1) mm = PR::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
         uint16_t sh, bh;
         float b, inv;
-        const bool need = qparams1<BITS>(PR::lo(mm), -PR::hi(mm), T, sh, bh, b, inv);
+        const bool need = qparams1<BITS>(PR::lo(mm), -PR::hi(mm), sh, bh, b, inv);
         if (j == 0) {
             reinterpret_cast<uint16_t*>(rec + F::OFF_VS)[r] = sh;
             reinterpret_cast<uint16_t*>(rec + F::OFF_VB)[r] = bh;
@@ -645,7 +639,7 @@ __device__ __forceinline__ void k_encode(const uint32_t (&w)[WS<D, BITS, P, IN>:
 // the warp's K code bytes [wg DCW, (wg + 1) DCW) of a full page from the slot: per-channel ranges over the P rows,
 // then the codes
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, const uint32_t* T, int lane, int wg) {
+__device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, int lane, int wg) {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
@@ -715,7 +709,7 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, con
                 lo_ = f2_of<IN>(a0);
                 hi_ = f2_of<IN>(m0);
             }
-            need |= qparams2<BITS>(lo_, hi_, T, sh[o], bh[o], bo[o], ivo[o]);
+            need |= qparams2<BITS>(lo_, hi_, sh[o], bh[o], bo[o], ivo[o]);
         }
         if (set * OWN < NPR) {
             const int q0 = set * OWN;
@@ -800,12 +794,9 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
     using C = WS<D, BITS, P, IN>;
     constexpr int FULL = 1 << 30;
     extern __shared__ __align__(128) uint8_t wsm[];
-    uint32_t* T = reinterpret_cast<uint32_t*>(wsm);
     uint64_t* bars = reinterpret_cast<uint64_t*>(wsm + C::OFF_BAR);
     const int lane = threadIdx.x % WARP, w = threadIdx.x / WARP;
     const int st = w / C::G, wg = w % C::G;                          // item stream of the CTA, warp within it
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
-        T[i] = __float_as_uint(__frcp_rn(1.0f + float(i) * (1.0f / 1024.0f)));
     volatile int* stop = reinterpret_cast<volatile int*>(wsm + C::OFF_STOP);
     if (threadIdx.x < C::NST * C::NS) mbar_init(&bars[threadIdx.x], 1);
     if (threadIdx.x < C::NST) stop[threadIdx.x] = 0;
@@ -923,8 +914,8 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
                 phase ^= 1u << slot;
                 const uint8_t* kbuf = slots + slot * C::STAGE;
                 uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
-                ws_v_rows<D, BITS, P, IN>(kbuf + P * C::RSTR, rec, T, lane, wg);
-                ws_k_page<D, BITS, P, IN>(kbuf, rec, T, lane, wg);
+                ws_v_rows<D, BITS, P, IN>(kbuf + P * C::RSTR, rec, lane, wg);
+                ws_k_page<D, BITS, P, IN>(kbuf, rec, lane, wg);
             }
         } else if (wg == 0) {
             general(i, l, h, blk);
@@ -1029,13 +1020,9 @@ int launch_write(const void* k_new, const void* v_new, int64_t k_stride, int64_t
 
 // Exhaustive check of the scale arithmetic of the streaming write against CUDA's IEEE operations: div_levels and
 // the packed div_levels2 (every value through both lanes) for every fp32 d in [2^-100, 2^100] (and 0), BITS 4 and
-// 8, against __fdiv_rn; rcp_fp16 for every fp16 bit pattern against `s > 0 ? __frcp_rn(s) : 0`.  Mismatch counts in
+// 8, against __fdiv_rn; rcp_nr for every fp16 bit pattern against `s > 0 ? __frcp_rn(s) : 0`.  Mismatch counts in
 // bad[0..2].
 __global__ void __launch_bounds__(256) selfcheck_kernel(unsigned long long* bad) {
-    __shared__ uint32_t T[1024];
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
-        T[i] = __float_as_uint(__frcp_rn(1.0f + float(i) * (1.0f / 1024.0f)));
-    __syncthreads();
     const uint32_t lo = 0x0D800000u, hi = 0x71800000u;          // 2^-100 .. 2^100
     unsigned long long b4 = 0, b8 = 0, br = 0;
     const uint32_t stride = gridDim.x * blockDim.x;
@@ -1053,17 +1040,14 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(unsigned long long* bad)
         b4 += div_levels<4>(0.0f) != 0.0f || div_levels2<4>(make_float2(0.0f, 0.0f)).x != 0.0f;
         b8 += div_levels<8>(0.0f) != 0.0f || div_levels2<8>(make_float2(0.0f, 0.0f)).y != 0.0f;
     }
-    unsigned long long bn = 0;
     for (uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < 65536u; p += stride) {
         const float sv = __half2float(__ushort_as_half(uint16_t(p)));
         const float want = sv > 0.0f ? __frcp_rn(sv) : 0.0f;
-        br += __float_as_uint(rcp_fp16(sv, T)) != __float_as_uint(want);
-        bn += __float_as_uint(rcp_nr(sv)) != __float_as_uint(want);
+        br += __float_as_uint(rcp_nr(sv)) != __float_as_uint(want);
     }
     if (b4) atomicAdd(&bad[0], b4);
     if (b8) atomicAdd(&bad[1], b8);
     if (br) atomicAdd(&bad[2], br);
-    if (bn) atomicAdd(&bad[3], bn);
 }
 
 int write_error_flag(int clear) {
@@ -1126,8 +1110,8 @@ extern "C" int kush_sm100_write(int32_t head_dim, int32_t bits, int32_t page, in
 extern "C" int kush_sm100_selfcheck(uint64_t* mismatches) {
     if (!mismatches) return set_error(KUSH_ERR_ARG, "kush_sm100_selfcheck: null pointer");
     unsigned long long* d = nullptr;
-    cudaError_t e = cudaMalloc(&d, 4 * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMemset(d, 0, 4 * sizeof(unsigned long long));
+    cudaError_t e = cudaMalloc(&d, 3 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(d, 0, 3 * sizeof(unsigned long long));
     if (e == cudaSuccess) {
         int sms = 0;
         int dev = 0;
@@ -1136,7 +1120,7 @@ extern "C" int kush_sm100_selfcheck(uint64_t* mismatches) {
         selfcheck_kernel<<<(sms > 0 ? sms : 1) * 8, 256>>>(d);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(mismatches, d, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     if (d) cudaFree(d);
     if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "kush_sm100_selfcheck: %s", cudaGetErrorString(e));
     return KUSH_OK;
