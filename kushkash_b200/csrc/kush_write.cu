@@ -636,48 +636,57 @@ __device__ __forceinline__ void k_encode(const uint32_t (&w)[WS<D, BITS, P, IN>:
     }
 }
 
-// the warp's K code bytes [wg DCW, (wg + 1) DCW) of a full page from the slot: per-channel ranges over the P rows,
-// then the codes
+// The warp's K code bytes [wg DCW, (wg + 1) DCW) of a full page from the slot, in three phases (ranges, scale
+// parameters, codes) so that a caller can interleave them with the V rows' phases.
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, int lane, int wg) {
+struct KPage {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
-    constexpr int KWD = C::KWD, NU = C::NU, NPR = C::NPR;
-    constexpr int TR = C::KREG ? C::TPS : 1;                         // rows whose words stay in registers
-    const int c = lane % C::LW, t0 = (lane / C::LW) * C::TPS;
-    const int e0 = wg * C::DCW + c * C::KC;                          // first code byte of the lane
-    uint32_t kw[TR][KWD];
-    uint32_t mn[KWD], mx[KWD];
-    ws_k_words<D, BITS, P, IN>(kbuf, t0, e0, kw[0]);
-#pragma unroll
-    for (int i = 0; i < KWD; i++) mn[i] = mx[i] = kw[0][i];
-#pragma unroll
-    for (int t = 1; t < C::TPS; t++) {
-        uint32_t w[KWD];
-        ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, e0, w);
-#pragma unroll
-        for (int i = 0; i < KWD; i++) {
-            if constexpr (C::KREG) kw[t < TR ? t : 0][i] = w[i];
-            mn[i] = PR::min2(mn[i], w[i]);
-            mx[i] = PR::max2(mx[i], w[i]);
-        }
+    static constexpr int KWD = C::KWD, NU = C::NU, NPR = C::NPR;
+    static constexpr int TR = C::KREG ? C::TPS : 1;                  // rows whose words stay in registers
+    static constexpr int OWN = NPR >= C::TS ? NPR / C::TS : 1;       // channel pairs whose scales a lane computes
+    const uint8_t* kbuf;
+    int lane, t0, e0;
+    uint32_t kw[TR][KWD], mn[KWD], mx[KWD];
+    float2 b[NPR], iv[NPR];
+    bool need;
+
+    __device__ __forceinline__ KPage(const uint8_t* kb, int lane_, int wg) : kbuf(kb), lane(lane_), need(false) {
+        t0 = (lane / C::LW) * C::TPS;
+        e0 = wg * C::DCW + (lane % C::LW) * C::KC;                   // first code byte of the lane
     }
+
+    // per-channel (min, max) over the P rows: in-lane over the set's TPS rows, then across the TS sets
+    __device__ __forceinline__ void ranges() {
+        ws_k_words<D, BITS, P, IN>(kbuf, t0, e0, kw[0]);
 #pragma unroll
-    for (int o = C::LW; o < 32; o <<= 1)
+        for (int i = 0; i < KWD; i++) mn[i] = mx[i] = kw[0][i];
 #pragma unroll
-        for (int i = 0; i < KWD; i++) {
-            mn[i] = PR::min2(mn[i], __shfl_xor_sync(0xffffffffu, mn[i], o));
-            mx[i] = PR::max2(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
+        for (int t = 1; t < C::TPS; t++) {
+            uint32_t w[KWD];
+            ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, e0, w);
+#pragma unroll
+            for (int i = 0; i < KWD; i++) {
+                if constexpr (C::KREG) kw[t < TR ? t : 0][i] = w[i];
+                mn[i] = PR::min2(mn[i], w[i]);
+                mx[i] = PR::max2(mx[i], w[i]);
+            }
         }
+#pragma unroll
+        for (int o = C::LW; o < 32; o <<= 1)
+#pragma unroll
+            for (int i = 0; i < KWD; i++) {
+                mn[i] = PR::min2(mn[i], __shfl_xor_sync(0xffffffffu, mn[i], o));
+                mx[i] = PR::max2(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
+            }
+    }
+
     // channel pairs: int4 pair q = (lo dim e0 + q, hi dim e0 + q); int8 pair q = (dims e0 + 2q, e0 + 2q + 1).
     // The TS token sets hold the same ranges: set k computes pairs [k OWN, (k + 1) OWN), stores their scales and
     // biases, and every lane takes the other pairs' (bias, 1 / scale) from their owners by shuffles.
-    constexpr int OWN = NPR >= C::TS ? NPR / C::TS : 1;
-    const int set = lane / C::LW;
-    float2 b[NPR], iv[NPR];
-    bool need = false;
-    {
+    __device__ __forceinline__ void params(uint8_t* rec) {
+        const int set = lane / C::LW;
         float2 bo[OWN], ivo[OWN];
         uint32_t sh[OWN], bh[OWN];
 #pragma unroll
@@ -748,20 +757,61 @@ __device__ __forceinline__ void ws_k_page(const uint8_t* kbuf, uint8_t* rec, int
                                 __shfl_sync(0xffffffffu, ivo[q % OWN].y, src));
         }
     }
-    uint8_t* dst = rec + t0 * F::DC + e0;
-    const bool cl = __any_sync(0xffffffffu, need);
+
+    __device__ __forceinline__ void codes(uint8_t* rec) {
+        uint8_t* dst = rec + t0 * F::DC + e0;
+        const bool cl = __any_sync(0xffffffffu, need);
 #pragma unroll
-    for (int t = 0; t < C::TPS; t++) {
-        uint32_t w[KWD];
-        if constexpr (C::KREG) {
+        for (int t = 0; t < C::TPS; t++) {
+            uint32_t w[KWD];
+            if constexpr (C::KREG) {
 #pragma unroll
-            for (int i = 0; i < KWD; i++) w[i] = kw[t][i];
-        } else {
-            ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, e0, w);
+                for (int i = 0; i < KWD; i++) w[i] = kw[t][i];
+            } else {
+                ws_k_words<D, BITS, P, IN>(kbuf, t0 + t, e0, w);
+            }
+            if (cl) k_encode<D, BITS, P, IN, true>(w, b, iv, dst + t * F::DC);
+            else k_encode<D, BITS, P, IN, false>(w, b, iv, dst + t * F::DC);
         }
-        if (cl) k_encode<D, BITS, P, IN, true>(w, b, iv, dst + t * F::DC);
-        else k_encode<D, BITS, P, IN, false>(w, b, iv, dst + t * F::DC);
     }
+};
+
+// One full page of one kv head from the slot (this warp's share): V rows and K page phases interleaved -- ranges,
+// then every scale parameter (independent chains), then the codes.
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void ws_item(const uint8_t* kbuf, uint8_t* rec, int lane, int wg) {
+    using C = WS<D, BITS, P, IN>;
+    using F = typename C::F;
+    using PR = Pair16<IN>;
+    KPage<D, BITS, P, IN> kp(kbuf, lane, wg);
+    if constexpr (C::VPASS == 1) {
+        const int j = lane % C::GL, r = 16 * wg + lane / C::GL;
+        uint32_t w[C::VW];
+        v_words<D, BITS, P, IN>(kbuf + (P + r) * C::RSTR, j, w);
+        uint32_t m, M;
+        range_tree<IN, C::VW>(w, m, M);
+        const uint32_t nM = M ^ 0x80008000u;                        // -max: both ranges reduce as one min
+        uint32_t mm = PR::min2(prmt(m, nM, 0x5410), prmt(m, nM, 0x7632));       // (min, -max)
+#pragma unroll
+        for (int o = C::GL / 2; o; o >>= 1) mm = PR::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        kp.ranges();
+        uint16_t sh, bh;
+        float b, inv;
+        const bool need = qparams1<BITS>(PR::lo(mm), -PR::hi(mm), sh, bh, b, inv);
+        kp.params(rec);
+        if (j == 0) {
+            reinterpret_cast<uint16_t*>(rec + F::OFF_VS)[r] = sh;
+            reinterpret_cast<uint16_t*>(rec + F::OFF_VB)[r] = bh;
+        }
+        uint8_t* dst = rec + F::OFF_VQ + r * F::DC + j * (F::DC / C::GL);
+        if (__any_sync(0xffffffffu, need)) v_encode<D, BITS, P, IN, true>(w, b, inv, dst);
+        else v_encode<D, BITS, P, IN, false>(w, b, inv, dst);
+    } else {
+        ws_v_rows<D, BITS, P, IN>(kbuf + P * C::RSTR, rec, lane, wg);
+        kp.ranges();
+        kp.params(rec);
+    }
+    kp.codes(rec);
 }
 
 // job metadata of one item, one item per lane (see write_stream_kernel); hf = kv head | full << 30
@@ -914,8 +964,7 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
                 phase ^= 1u << slot;
                 const uint8_t* kbuf = slots + slot * C::STAGE;
                 uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
-                ws_v_rows<D, BITS, P, IN>(kbuf + P * C::RSTR, rec, lane, wg);
-                ws_k_page<D, BITS, P, IN>(kbuf, rec, lane, wg);
+                ws_item<D, BITS, P, IN>(kbuf, rec, lane, wg);
             }
         } else if (wg == 0) {
             general(i, l, h, blk);
