@@ -465,36 +465,42 @@ __device__ __forceinline__ bool qparams1(float mn, float mx, uint16_t& sh, uint1
     return !(ylo >= LO && yhi < HI);
 }
 
-// Streaming-write geometry.  An item (one page of one kv head) is handled by G = P / 16 warps sharing one ring
-// slot: warp wg of the group encodes V rows [16 wg, 16 wg + 16) and code bytes [wg DCW, (wg + 1) DCW) of the K rows.
+// Streaming-write geometry.  An item is one page of one kv head.  P = 16: one warp encodes the item's V rows and
+// K page from one ring slot.  P = 32: two warps take the item, warp 0 its V rows and warp 1 its K page, each from
+// its own ring of slots holding only the rows it encodes (no slot is shared, so the two never wait on each other).
 template <int D, int BITS, int P, class IN>
 struct WS {
     using F = Fmt<D, BITS, P>;
     static constexpr int G = P / 16;                                // warps per item
     static constexpr int ROWB = 2 * D;                              // bytes of an input row
     static constexpr int RSTR = ROWB + 16;                          // slot row stride (skews banks across rows)
-    static constexpr int STAGE = 2 * P * RSTR;                      // one slot: P K rows, then P V rows
-    static constexpr int NS = 2;                                    // ring slots per item stream
-    static constexpr int NW = (4 / G) * NS * STAGE <= 73728 ? 4 : G > 1 ? G : 2;           // warps per CTA
+    // K: lane = KC code bytes of a row (int4: KC lo dims + KC hi dims; int8: KC dims), LW lanes per token set, TS
+    // token sets of TPS rows (ranges combined across sets by shuffles)
+    static constexpr int DC = F::DC;
+    static constexpr int KC = DC / 32 > 4 ? DC / 32 : 4;
+    static constexpr int LW = DC / KC, TS = 32 / LW, TPS = P / TS;
+    // slot: K rows (the rows of token set k shifted by k KGAP bytes: the sets read in one shared-memory wavefront
+    // then hit disjoint banks) unless the warp encodes V only, then the V rows from VOFF unless it encodes K only
+    static constexpr int KGAP = 8 * LW;
+    static constexpr int KBYTES = P * RSTR + (TS - 1) * KGAP;
+    static constexpr int VOFF = G == 1 ? KBYTES : 0;
+    static constexpr int STAGE = G == 1 ? KBYTES + P * RSTR : (KBYTES > P * RSTR ? KBYTES : P * RSTR);
+    static constexpr int NS = 2;                                    // ring slots per warp
+    static constexpr int NW = 4 * NS * STAGE <= 73728 ? 4 : 2;      // warps per CTA
     static constexpr int NST = NW / G;                              // item streams per CTA
-    static constexpr int OFF_BAR = 0;                               // NST * NS mbarriers
-    static constexpr int OFF_STOP = 64;                             // per stream: a wait gave up
+    static constexpr int OFF_BAR = 0;                               // full[NW][NS]
     static constexpr int OFF_STAGE = 128;
-    static constexpr int SMEM = OFF_STAGE + NST * NS * STAGE;
+    static constexpr int SMEM = OFF_STAGE + NW * NS * STAGE;
     // V: GL lanes per row, VPL values per lane (int4: VPL/2 lo dims + the matching hi dims), RPP rows per pass
     static constexpr int GL = D / 64 > 2 ? D / 64 : 2;
-    static constexpr int VPL = D / GL, VW = VPL / 2, RPP = 32 / GL, VPASS = 16 / RPP;
-    // K: lane = KC code bytes of a row (int4: KC lo dims + KC hi dims; int8: KC dims) within the warp's DCW bytes,
-    // LW lanes per token set, TS token sets of TPS rows (ranges combined across sets by shuffles)
-    static constexpr int DC = F::DC;
-    static constexpr int DCW = DC / G;
-    static constexpr int KC = DCW / 32 > 4 ? DCW / 32 : 4;
-    static constexpr int LW = DCW / KC, TS = 32 / LW, TPS = P / TS;
+    static constexpr int VPL = D / GL, VW = VPL / 2, RPP = 32 / GL, VPASS = P / RPP;
     static constexpr int NU = KC / 2;                               // 2-byte code units per row per lane
     static constexpr int KWD = BITS == 4 ? KC : KC / 2;             // input words per row per lane
     static constexpr int NPR = BITS == 4 ? 2 * NU : NU;             // channel pairs per lane
     static constexpr bool KREG = TPS * KWD <= 32;                   // keep the K words in registers between passes
-    static_assert(P == 16 * G && NW % G == 0 && RPP * VPASS == 16 && (G == 1 || NST <= 2), "geometry");
+    __host__ __device__ static constexpr int kpos(int t) { return t * RSTR + (t / TPS) * KGAP; }
+    static_assert(P == 16 * G && NW % G == 0 && P % RPP == 0 && NW * NS * 8 <= OFF_STAGE && VOFF % 16 == 0,
+                  "geometry");
 };
 
 // the VW words of V row `row` this lane encodes: int4: lo dims [j VPL/2, (j+1) VPL/2), then the same hi dims;
@@ -561,16 +567,16 @@ __device__ __forceinline__ void range_tree(const uint32_t (&w)[N], uint32_t& m, 
     M = b[0];
 }
 
-// the warp's 16 V rows of a full page from the slot: row 16 wg + pass RPP + lane / GL, lane part j = lane % GL
+// the V rows of a full page from the slot: row pass RPP + lane / GL, lane part j = lane % GL
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, int lane, int wg) {
+__device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, int lane) {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
     const int j = lane % C::GL;
 #pragma unroll 1
     for (int pass = 0; pass < C::VPASS; pass++) {
-        const int r = 16 * wg + pass * C::RPP + lane / C::GL;
+        const int r = pass * C::RPP + lane / C::GL;
         uint32_t w[C::VW];
         v_words<D, BITS, P, IN>(vbuf + r * C::RSTR, j, w);
         uint32_t m, M;
@@ -597,7 +603,7 @@ __device__ __forceinline__ void ws_v_rows(const uint8_t* vbuf, uint8_t* rec, int
 template <int D, int BITS, int P, class IN>
 __device__ __forceinline__ void ws_k_words(const uint8_t* kbuf, int t, int e0, uint32_t (&w)[WS<D, BITS, P, IN>::KWD]) {
     using C = WS<D, BITS, P, IN>;
-    const uint8_t* row = kbuf + t * C::RSTR + 2 * e0;
+    const uint8_t* row = kbuf + C::kpos(t) + 2 * e0;
     if constexpr (C::KC == 4) {
         const uint2 a = *reinterpret_cast<const uint2*>(row);
         w[0] = a.x;
@@ -636,8 +642,8 @@ __device__ __forceinline__ void k_encode(const uint32_t (&w)[WS<D, BITS, P, IN>:
     }
 }
 
-// The warp's K code bytes [wg DCW, (wg + 1) DCW) of a full page from the slot, in three phases (ranges, scale
-// parameters, codes) so that a caller can interleave them with the V rows' phases.
+// The K page of a full page from the slot, in three phases (ranges, scale parameters, codes) so that a caller can
+// interleave them with the V rows' phases.
 template <int D, int BITS, int P, class IN>
 struct KPage {
     using C = WS<D, BITS, P, IN>;
@@ -652,9 +658,9 @@ struct KPage {
     float2 b[NPR], iv[NPR];
     bool need;
 
-    __device__ __forceinline__ KPage(const uint8_t* kb, int lane_, int wg) : kbuf(kb), lane(lane_), need(false) {
+    __device__ __forceinline__ KPage(const uint8_t* kb, int lane_) : kbuf(kb), lane(lane_), need(false) {
         t0 = (lane / C::LW) * C::TPS;
-        e0 = wg * C::DCW + (lane % C::LW) * C::KC;                   // first code byte of the lane
+        e0 = (lane % C::LW) * C::KC;                                 // first code byte of the lane
     }
 
     // per-channel (min, max) over the P rows: in-lane over the set's TPS rows, then across the TS sets
@@ -776,18 +782,27 @@ struct KPage {
     }
 };
 
-// One full page of one kv head from the slot (this warp's share): V rows and K page phases interleaved -- ranges,
-// then every scale parameter (independent chains), then the codes.
+// One full page of one kv head from the slot, this warp's share (role 0: V rows, 1: K page; P = 16: both, the
+// V and K phases interleaved -- ranges, then every scale parameter (independent chains), then the codes).
 template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void ws_item(const uint8_t* kbuf, uint8_t* rec, int lane, int wg) {
+__device__ __forceinline__ void ws_item(const uint8_t* buf, uint8_t* rec, int lane, int role) {
     using C = WS<D, BITS, P, IN>;
     using F = typename C::F;
     using PR = Pair16<IN>;
-    KPage<D, BITS, P, IN> kp(kbuf, lane, wg);
-    if constexpr (C::VPASS == 1) {
-        const int j = lane % C::GL, r = 16 * wg + lane / C::GL;
+    if constexpr (C::G == 2) {
+        if (role == 0) {
+            ws_v_rows<D, BITS, P, IN>(buf, rec, lane);
+        } else {
+            KPage<D, BITS, P, IN> kp(buf, lane);
+            kp.ranges();
+            kp.params(rec);
+            kp.codes(rec);
+        }
+    } else if constexpr (C::VPASS == 1) {
+        KPage<D, BITS, P, IN> kp(buf, lane);
+        const int j = lane % C::GL, r = lane / C::GL;
         uint32_t w[C::VW];
-        v_words<D, BITS, P, IN>(kbuf + (P + r) * C::RSTR, j, w);
+        v_words<D, BITS, P, IN>(buf + C::VOFF + r * C::RSTR, j, w);
         uint32_t m, M;
         range_tree<IN, C::VW>(w, m, M);
         const uint32_t nM = M ^ 0x80008000u;                        // -max: both ranges reduce as one min
@@ -806,12 +821,14 @@ __device__ __forceinline__ void ws_item(const uint8_t* kbuf, uint8_t* rec, int l
         uint8_t* dst = rec + F::OFF_VQ + r * F::DC + j * (F::DC / C::GL);
         if (__any_sync(0xffffffffu, need)) v_encode<D, BITS, P, IN, true>(w, b, inv, dst);
         else v_encode<D, BITS, P, IN, false>(w, b, inv, dst);
+        kp.codes(rec);
     } else {
-        ws_v_rows<D, BITS, P, IN>(kbuf + P * C::RSTR, rec, lane, wg);
+        ws_v_rows<D, BITS, P, IN>(buf + C::VOFF, rec, lane);
+        KPage<D, BITS, P, IN> kp(buf, lane);
         kp.ranges();
         kp.params(rec);
+        kp.codes(rec);
     }
-    kp.codes(rec);
 }
 
 // job metadata of one item, one item per lane (see write_stream_kernel); hf = kv head | full << 30
@@ -819,22 +836,8 @@ struct WMeta {
     int row0, hf, blk, s, pg, q0, ctx, total;
 };
 
-// the G warps of an item stream: one warp syncs itself, a pair of warps takes named barrier 1 + stream (immediate
-// ids: the kernel reserves only the barriers it names)
-template <int G>
-__device__ __forceinline__ void group_sync(int stream) {
-    static_assert(G == 1 || G == 2, "one or two warps per item");
-    if constexpr (G == 1) {
-        __syncwarp();
-    } else if (stream == 0) {
-        asm volatile("bar.sync 1, 64;" ::: "memory");
-    } else {
-        asm volatile("bar.sync 2, 64;" ::: "memory");
-    }
-}
-
 template <int D, int BITS, int P, class IN>
-__global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
+__global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
     write_stream_kernel(const IN* __restrict__ k_new, const IN* __restrict__ v_new, int64_t k_stride, int64_t v_stride,
                         const int32_t* __restrict__ qsl, const int32_t* __restrict__ seq_lens,
                         const int32_t* __restrict__ tail_idx, const int32_t* __restrict__ job_seq,
@@ -843,18 +846,16 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
                         int H, int n_jobs) {
     using C = WS<D, BITS, P, IN>;
     constexpr int FULL = 1 << 30;
-    extern __shared__ __align__(128) uint8_t wsm[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(wsm + C::OFF_BAR);
+    extern __shared__ __align__(128) uint8_t wss[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wss + C::OFF_BAR);
     const int lane = threadIdx.x % WARP, w = threadIdx.x / WARP;
-    const int st = w / C::G, wg = w % C::G;                          // item stream of the CTA, warp within it
-    volatile int* stop = reinterpret_cast<volatile int*>(wsm + C::OFF_STOP);
-    if (threadIdx.x < C::NST * C::NS) mbar_init(&bars[threadIdx.x], 1);
-    if (threadIdx.x < C::NST) stop[threadIdx.x] = 0;
+    const int st = w / C::G, role = w % C::G;                        // item stream of the CTA, role in it
+    if (threadIdx.x < C::NW * C::NS) mbar_init(&bars[threadIdx.x], 1);                   // full: the issuing lane
     fence_mbar_init();
     __syncthreads();
 
-    uint8_t* slots = wsm + C::OFF_STAGE + st * C::NS * C::STAGE;
-    const uint32_t bar0 = smem_u32(&bars[st * C::NS]);
+    uint8_t* slots = wss + C::OFF_STAGE + w * C::NS * C::STAGE;      // this warp's ring
+    const uint32_t bar0 = smem_u32(&bars[w * C::NS]);
     const int64_t n_items = int64_t(n_jobs) * H;
     const int64_t TW = int64_t(gridDim.x) * C::NST;
     const int64_t first = int64_t(blockIdx.x) * C::NST + st;
@@ -880,26 +881,31 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
     };
     WMeta cur = load_meta(0), nxt = load_meta(1);
 #define KUSH_META(field, use_b, l) __shfl_sync(0xffffffffu, (use_b) ? nxt.field : cur.field, (l))
-    // warp 0 of the stream brings the rows of full item i (first input row row0, kv head h) into slot i % NS
+    // bring the rows of full item i (first input row row0, kv head h) this warp encodes into its slot i % NS:
+    // P = 16 K and V rows; P = 32 the V rows (role 0) or the K rows (role 1)
     auto issue = [&](int i, int row0, int h) {
+        constexpr int NR = C::G == 1 ? 2 * P : P;
         const uint32_t bar = bar0 + 8u * uint32_t(i % C::NS);
         const uint32_t dst = smem_u32(slots + (i % C::NS) * C::STAGE);
         if (lane == 0)
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(uint32_t(2 * P * C::ROWB))
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(uint32_t(NR * C::ROWB))
                          : "memory");
         __syncwarp();
 #pragma unroll
-        for (int r = lane; r < 2 * P; r += WARP) {
-            const IN* src = r < P ? k_new + (int64_t(row0) + r) * k_stride + int64_t(h) * D
-                                  : v_new + (int64_t(row0) + r - P) * v_stride + int64_t(h) * D;
+        for (int r = lane; r < NR; r += WARP) {
+            const bool is_k = C::G == 1 ? r < P : role == 1;
+            const int t = C::G == 1 && r >= P ? r - P : r;           // token row of the page
+            const IN* src = is_k ? k_new + (int64_t(row0) + t) * k_stride + int64_t(h) * D
+                                 : v_new + (int64_t(row0) + t) * v_stride + int64_t(h) * D;
+            const uint32_t off = is_k ? C::kpos(t) : C::VOFF + t * C::RSTR;
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                             dst + uint32_t(r * C::RSTR)),
+                             dst + off),
                          "l"(src), "r"(uint32_t(C::ROWB)), "r"(bar)
                          : "memory");
         }
     };
-    // every other item: the warp-level per-token path (mode 0 / 1 / 2 as write_kernel) by warp 0 of the stream,
-    // slot i % NS as scratch
+    // every other item: the warp-level per-token path (mode 0 / 1 / 2 as write_kernel) by the role-0 warp of the
+    // stream, its slot i % NS as scratch
     auto general = [&](int i, int l, int h, int blk) {
         const int64_t ps = int64_t(KUSH_META(pg, false, l)) * P, ctx = KUSH_META(ctx, false, l);
         const int64_t total = KUSH_META(total, false, l), q0 = KUSH_META(q0, false, l);
@@ -936,55 +942,53 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the slot may next be filled by a bulk copy
     };
 
-    if (wg == 0) {
-        for (int i = 0; i < C::NS - 1 && i < n_local; i++) {
-            const int hf = KUSH_META(hf, false, i);
-            if (hf & FULL) issue(i, KUSH_META(row0, false, i), hf & (FULL - 1));
+    // full[slot] completes one phase per FULL item of the slot (general items are never issued): phase bit per
+    // slot, flipped at each completed wait; the slots with copies in flight are kept for the error path
+    uint32_t phase = 0, inflight = 0;
+    bool ok = true;
+    for (int i = 0; i < C::NS - 1 && i < n_local; i++) {
+        const int hf = KUSH_META(hf, false, i);
+        if (hf & FULL) {
+            issue(i, KUSH_META(row0, false, i), hf & (FULL - 1));
+            inflight |= 1u << (i % C::NS);
         }
     }
-    uint32_t phase = 0;
-    for (int i = 0; i < n_local; i++) {
+    for (int i = 0; i < n_local && ok; i++) {
         if (i % WARP == 0 && i) {
             cur = nxt;
             nxt = load_meta(i / WARP + 1);
         }
         const int ia = i + C::NS - 1;                                // the item whose rows start now
-        if (wg == 0 && ia < n_local) {
+        if (ia < n_local) {
             const bool nb = ia / WARP != i / WARP;
             const int hfa = KUSH_META(hf, nb, ia % WARP);
-            if (hfa & FULL) issue(ia, KUSH_META(row0, nb, ia % WARP), hfa & (FULL - 1));
+            if (hfa & FULL) {
+                issue(ia, KUSH_META(row0, nb, ia % WARP), hfa & (FULL - 1));
+                inflight |= 1u << (ia % C::NS);
+            }
         }
         const int l = i % WARP;
         const int hf = KUSH_META(hf, false, l), blk = KUSH_META(blk, false, l);
         const int h = hf & (FULL - 1), slot = i % C::NS;
-        bool ok = true;
         if (hf & FULL) {
             ok = __all_sync(0xffffffffu, mbar_wait_u32(bar0 + 8u * slot, (phase >> slot) & 1u));
             if (ok) {
                 phase ^= 1u << slot;
-                const uint8_t* kbuf = slots + slot * C::STAGE;
-                uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
-                ws_item<D, BITS, P, IN>(kbuf, rec, lane, wg);
+                inflight &= ~(1u << slot);
+                ws_item<D, BITS, P, IN>(slots + slot * C::STAGE, rec_at(cache, blk, h, block_stride, head_stride),
+                                        lane, role);
             }
-        } else if (wg == 0) {
+        } else if (role == 0) {
             general(i, l, h, blk);
         }
-        if (!ok && lane == 0) {
-            atomicExch(&g_write_error, 1);
-            stop[st] = 1;
-        }
-        group_sync<C::G>(st);                                        // the slot is free for the next issue
-        if (stop[st]) {
-            // a copy never completed: warp 0 waits (bounded) for the stream's other copies, then the stream stops
-            if (wg == 0) {
-                for (int k = i + 1; k < i + C::NS && k < n_local; k++) {
-                    const int sk = k % C::NS;
-                    if (KUSH_META(hf, k / WARP != i / WARP, k % WARP) & FULL)
-                        mbar_wait_u32(bar0 + 8u * sk, ((phase >> sk) & 1u));
-                }
-            }
-            return;
-        }
+        __syncwarp();
+    }
+    if (!ok) {
+        // a copy never completed: record it, wait (bounded) for this warp's copies still in flight, stop
+        if (lane == 0) atomicExch(&g_write_error, 1);
+#pragma unroll
+        for (int sl = 0; sl < C::NS; sl++)
+            if (inflight >> sl & 1u) mbar_wait_u32(bar0 + 8u * sl, (phase >> sl) & 1u);
     }
 #undef KUSH_META
 }
