@@ -16,6 +16,8 @@ algorithmic bytes / its CUDA-event duration vs the measured HBM copy peak); the 
 (cpu_baseline); clocks sampled with nvidia-smi during the timed region.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
+    python bench.py --workload long           # BASELINE config 4 (kv heads partitioned over the GPUs)
+    python bench.py --workload mix            # BASELINE config 5 (serving mix: prompt writes + ragged decode)
     python bench.py --impl reference          # the reference's CPU algorithm (C restatement) on the host cores
     torchrun --nproc-per-node N bench.py --gpus N ...
 """
@@ -329,13 +331,16 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["batch", "long"], default="batch",
-                    help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned)")
+    ap.add_argument("--workload", choices=["batch", "long", "mix"], default="batch",
+                    help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned); "
+                         "mix: config 5 (serving mix, requests partitioned)")
     a = ap.parse_args()
     if a.workload == "long":
         for k, v in (("batch", 4), ("context", 131072), ("page", 32), ("layers", 8)):
             if getattr(a, k) == ap.get_default(k):
                 setattr(a, k, v)
+    if a.workload == "mix" and a.layers == ap.get_default("layers"):
+        a.layers = 4
     if a.warmup < 3 and a.impl == "ours":
         print("bench.py: --warmup < 3 is raised to 3 (timing rule)", file=sys.stderr)
         a.warmup = 3
@@ -349,6 +354,9 @@ def main() -> None:
         return
     if a.workload == "long":
         run_long(a, world, rank, local)
+        return
+    if a.workload == "mix":
+        run_mix(a, world, rank, local)
         return
 
     torch.cuda.set_device(local)
@@ -546,6 +554,267 @@ def run_long(a, world: int, rank: int, local: int) -> None:
             "decode_tokens_per_s": round(geo.B / (ms_step / 1e3), 1), "clocks": clocks,
             "gpu_launches": a.steps * eng.launches_per_step(), "cuda_graph": graph is not None}), flush=True)
     del graph, eng
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- config 5: serving mix
+MIX_SEQS, MIX_PROMPTS, MIX_PROMPT_LEN = 2048, 32, 2048
+
+
+def mix_lengths(seed: int = 5) -> list[int]:
+    """Context lengths of the 2048 decode sequences: lognormal, median 2048, sigma 0.8, capped at 16384 (seeded)."""
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(MIX_SEQS, generator=gen) * 0.8 + math.log(2048)
+    return [int(min(16384, max(1, round(math.exp(v))))) for v in x.tolist()]
+
+
+class MixEngine:
+    """BASELINE config 5 state on one GPU for this rank's share of the requests: L layers of the decode sequences'
+    caches (ragged lengths) plus the pages of this rank's share of the 32 prompts, and the per-step inputs."""
+
+    def __init__(self, lens: list[int], n_prompts: int, L: int, device: torch.device, seed: int, extra_tokens: int):
+        from kushkash_b200 import Ops
+        self.dev, self.L, self.lens, self.PR = device, L, lens, n_prompts
+        self.D, self.HKV, self.HQ, self.bits, self.P = 128, 8, 32, 4, 16
+        D, H, P = self.D, self.HKV, self.P
+        self.RB = 2 * P * (D // 2) + 4 * D + 4 * P
+        self.ops = Ops(device, D, self.bits, self.HQ // H, torch.bfloat16, P)
+        S = self.S = len(lens)
+        gen = torch.Generator().manual_seed(seed)
+        pages = torch.tensor([-(-(n + extra_tokens) // P) for n in lens], dtype=torch.int64)
+        ppr = MIX_PROMPT_LEN // P
+        n_blocks = int(pages.sum()) + n_prompts * ppr
+        perm = torch.randperm(n_blocks, generator=gen).to(torch.int32)
+        maxp = int(pages.max()) if S else 1
+        bt = torch.zeros(max(S, 1), maxp, dtype=torch.int32)
+        o = 0
+        for s, n in enumerate(pages.tolist()):
+            bt[s, :n] = perm[o:o + n]
+            o += n
+        self.bt_dec = bt.to(device)
+        self.bt_pr = perm[o:].view(n_prompts, ppr).to(device)
+        self.pool = torch.zeros(L, n_blocks, H, self.RB, dtype=torch.uint8, device=device)
+        self.tail_dec = torch.zeros(L, max(S, 1), H, P, D, dtype=torch.bfloat16, device=device)
+        self.tail_pr = torch.zeros(L, n_prompts, H, P, D, dtype=torch.bfloat16, device=device)
+        self.ti_dec = torch.arange(max(S, 1), dtype=torch.int32, device=device)
+        self.ti_pr = torch.arange(n_prompts, dtype=torch.int32, device=device)
+        self.sl_dec = torch.zeros(L, max(S, 1), dtype=torch.int32, device=device)
+        self.sl_pr = torch.full((n_prompts,), MIX_PROMPT_LEN, dtype=torch.int32, device=device)
+        self.offsets = (torch.randn(H, D, generator=gen) * 2).to(device)
+        for h in range(H):
+            idx = torch.randperm(D, generator=gen)[:2]
+            self.offsets[h, idx] = (15 * torch.sign(torch.randn(2, generator=gen))).to(device)
+        self.scale = 1.0 / math.sqrt(D)
+        self.ns = self.ops.splits(S, H, max(lens) // P) if S else 1
+        self.work = torch.empty(max(1, self.ops.work_size(max(S, 1), H, self.ns)), device=device)
+        dgen = torch.Generator(device=device).manual_seed(seed + 1)
+        self._fill(dgen)
+        # per-step inputs: the prompts' K/V per layer, one new token per decode sequence and layer, q; outputs
+        T = n_prompts * MIX_PROMPT_LEN
+        self.pk = (torch.randn(L, T, H, D, generator=dgen, device=device) + self.offsets).to(torch.bfloat16)
+        self.pv = torch.randn(L, T, H, D, generator=dgen, device=device).to(torch.bfloat16)
+        self.pqsl = torch.arange(n_prompts + 1, dtype=torch.int32, device=device) * MIX_PROMPT_LEN
+        self.pjs = torch.arange(n_prompts, dtype=torch.int32, device=device).repeat_interleave(ppr)
+        self.pjp = torch.arange(ppr, dtype=torch.int32, device=device).repeat(n_prompts)
+        self.k_new = (torch.randn(L, max(S, 1), H, D, generator=dgen, device=device) + self.offsets).to(torch.bfloat16)
+        self.v_new = torch.randn(L, max(S, 1), H, D, generator=dgen, device=device).to(torch.bfloat16)
+        self.q = torch.randn(L, max(S, 1), self.HQ, D, generator=dgen, device=device).to(torch.bfloat16)
+        self.out = torch.empty_like(self.q)
+
+    def _fill(self, dgen) -> None:
+        """Bulk quantize-on-write of every decode sequence's context, per layer, in ragged chunks of <= 256k tokens."""
+        D, H, P, dev = self.D, self.HKV, self.P, self.dev
+        lens = torch.tensor(self.lens, dtype=torch.int64)
+        chunks, cur, tok = [], [], 0
+        for s, n in enumerate(self.lens):
+            if cur and tok + n > 262144:
+                chunks.append(cur)
+                cur, tok = [], 0
+            cur.append(s)
+            tok += n
+        if cur:
+            chunks.append(cur)
+        for layer in range(self.L):
+            for ch in chunks:
+                rows = torch.zeros(self.S, dtype=torch.int64)
+                rows[ch] = lens[ch]
+                qsl = torch.cat([torch.zeros(1, dtype=torch.int64), rows.cumsum(0)]).to(torch.int32).to(dev)
+                npg = -(-lens[ch] // P)
+                js = torch.tensor(ch, dtype=torch.int64).repeat_interleave(npg)
+                start = torch.cat([torch.zeros(1, dtype=torch.int64), npg.cumsum(0)[:-1]]).repeat_interleave(npg)
+                jp = torch.arange(int(npg.sum())) - start
+                T = int(rows.sum())
+                k = (torch.randn(T, H, D, generator=dgen, device=dev) + self.offsets).to(torch.bfloat16)
+                v = torch.randn(T, H, D, generator=dgen, device=dev).to(torch.bfloat16)
+                self.sl_dec[layer, ch] = lens[ch].to(torch.int32).to(dev)
+                self.ops.write(k, v, qsl, self.sl_dec[layer], self.ti_dec, js.to(torch.int32).to(dev),
+                               jp.to(torch.int32).to(dev), self.pool[layer], self.bt_dec, self.tail_dec[layer])
+        torch.cuda.synchronize(dev)
+
+    def prefill(self, layer: int) -> None:
+        self.ops.write(self.pk[layer], self.pv[layer], self.pqsl, self.sl_pr, self.ti_pr, self.pjs, self.pjp,
+                       self.pool[layer], self.bt_pr, self.tail_pr[layer])
+
+    def decode_step(self, layer: int) -> None:
+        self.ops.append(self.k_new[layer], self.v_new[layer], self.sl_dec[layer], self.ti_dec, self.pool[layer],
+                        self.bt_dec, self.tail_dec[layer], pos_offset=0, advance=True)
+        self.ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.bt_dec, self.sl_dec[layer], self.ti_dec,
+                        self.tail_dec[layer], self.scale, self.ns, self.work)
+
+    def step(self) -> None:
+        """One step of every layer: bulk prefill-quantize of the prompts, append + decode of every sequence."""
+        for layer in range(self.L):
+            self.prefill(layer)
+            if self.S:
+                self.decode_step(layer)
+
+    def decode_bytes(self, extra: int) -> int:
+        """Packed-KV bytes of one decode layer-step with every sequence `extra` tokens past its initial length."""
+        full, tot = 0, 0
+        for n in self.lens:
+            f, r = divmod(n + extra, self.P)
+            tot += f * self.RB + r * (2 * self.D + self.D // 2 + 4)
+        return tot * self.HKV
+
+    def prefill_bytes(self) -> int:
+        """Algorithmic bytes of one prompt write: bf16 K and V in, records out."""
+        T = self.PR * MIX_PROMPT_LEN
+        return 2 * T * self.HKV * self.D * 2 + (T // self.P) * self.HKV * self.RB
+
+    def append_bytes(self) -> int:
+        """Per layer: k, v rows in (bf16), the V code row and scale/bias and the exact K tail row out."""
+        return self.S * self.HKV * (4 * self.D + self.D // 2 + 4 + 2 * self.D)
+
+    def launches_per_step(self) -> int:
+        return self.L * (1 + (2 + (1 if self.ns > 1 else 0) if self.S else 0))
+
+
+def run_mix(a, world: int, rank: int, local: int) -> None:
+    """BASELINE config 5 (whole-box serving mix): 2048 concurrent sequences with lognormal context lengths and, per
+    step, a bulk prefill-quantize of 32 new 2048-token prompts plus a one-token append and attention for every
+    sequence; requests (sequences and prompts) are partitioned over the GPUs by tokens, no collective in the step.
+    32 layers of caches (~236 GB) do not fit one B200, so a step covers a subset of L layers (every layer is the same
+    work) and the 32-layer figures are the measured layer-step time x 32."""
+    from kushkash_b200.shard import partition_requests
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    lens_all = mix_lengths()
+    mine = partition_requests(lens_all, world)[rank]
+    lens = [lens_all[i] for i in mine]
+    n_pr = MIX_PROMPTS // world
+    eng = MixEngine(lens, n_pr, a.layers, dev, seed=777 + rank, extra_tokens=a.warmup + 2 * a.steps + 8)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(a.warmup - 1):
+        eng.step()
+    graph = capture(eng.step, dev)
+    n_done = a.warmup - 1
+    barrier()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    byts = sum(eng.decode_bytes(n_done + i + 1) for i in range(a.steps)) if eng.S else 0
+    byts = (byts + a.steps * (eng.prefill_bytes() + eng.append_bytes())) * eng.L
+    n_done += a.steps
+    # per-kernel rooflines on this rank: prompt writes alone, decodes alone (graphs, CUDA events)
+    wgraph = capture(lambda: [eng.prefill(l) for l in range(eng.L)], dev)
+    dgraph = capture(lambda: [eng.ops.decode(eng.q[l], eng.out[l], eng.pool[l], eng.bt_dec, eng.sl_dec[l], eng.ti_dec,
+                                             eng.tail_dec[l], eng.scale, eng.ns, eng.work) for l in range(eng.L)], dev)
+    kern = {}
+    for name, gr, nbytes in (("write", wgraph, eng.prefill_bytes()), ("decode", dgraph, eng.decode_bytes(n_done)
+                                                                       + eng.S * eng.HQ * eng.D * 4)):
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record()
+        for _ in range(3):
+            gr.replay()
+        k1.record()
+        torch.cuda.synchronize(dev)
+        kms = k0.elapsed_time(k1) / (3 * eng.L)
+        kern[name] = (nbytes, kms)
+    # e2e: every step's inputs (prompt K/V, new tokens, q) from pinned host memory, outputs back
+    hin = {k: getattr(eng, k).cpu().pin_memory() for k in ("pk", "pv", "k_new", "v_new", "q")}
+    hout = torch.empty(eng.out.shape, dtype=eng.out.dtype).pin_memory()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(a.steps):
+        for k_, t in hin.items():
+            getattr(eng, k_).copy_(t, non_blocking=True)
+        graph.replay()
+        hout.copy_(eng.out, non_blocking=True)
+    x1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = x0.elapsed_time(x1)
+    e2e_bytes = (sum(eng.decode_bytes(n_done + i + 1) for i in range(a.steps)) if eng.S else 0)
+    e2e_bytes = (e2e_bytes + a.steps * (eng.prefill_bytes() + eng.append_bytes())) * eng.L
+    h2d = sum(t.numel() * t.element_size() for t in hin.values())
+    d2h = hout.numel() * hout.element_size()
+    if dist is not None:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = (float(x) for x in t.tolist())
+        b = torch.tensor([float(byts), float(e2e_bytes)], device=dev, dtype=torch.float64)
+        dist.all_reduce(b)
+        byts, e2e_bytes = (float(x) for x in b.tolist())
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        ms_step = ms / a.steps
+        layer_us = ms_step * 1e3 / eng.L
+        value = byts / (ms / 1e3) / 1e9
+        roof = {}
+        for name, (nb, kms) in kern.items():
+            ach = nb / (kms / 1e3) / 1e9
+            roof[name] = {"kernel": f"kush_sm100_{name}", "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
+                          "algorithmic_bytes_per_launch": nb, "us_per_launch": round(kms * 1e3, 2), "rank": 0}
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
+            "data": "synthetic (seeded bf16 N(0,1) K/V/q, key offsets N(0, 2) + 2 outlier channels at +-15, lognormal "
+                    "lengths; BASELINE config 5 shapes)",
+            "config": {"workload": "BASELINE config 5: Llama-3.1-8B attention geometry, int4, page 16, 2048 sequences "
+                                   "(lognormal lengths, median 2048, sigma 0.8, cap 16384) + per step 32 prompts of "
+                                   f"2048 tokens; {eng.L} of the 32 layers per step (all layers are the same work)",
+                       "model": "Llama-3.1-8B (attention geometry only: 32 q heads, 8 kv heads, head_dim 128)",
+                       "global_batch": MIX_SEQS, "prompts_per_step": MIX_PROMPTS, "prompt_len": MIX_PROMPT_LEN,
+                       "cached_tokens": sum(lens_all), "layers_timed": eng.L, "page": 16, "bits": 4,
+                       "parallelism": f"requests partitioned over {world} GPU(s) by tokens, no collective in the step",
+                       "l2": "inputs larger than L2 (GBs of records per layer-step, no flush needed)"},
+            "value_is": "all bytes of the step (decode packed-KV reads + prompt bf16 in / records out + appends) over "
+                        "the max-over-ranks device time",
+            "per_gpu_gbs": round(value / world, 1),
+            "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
+            "us_per_layer_step": round(layer_us, 2),
+            "decode_tokens_per_s": round(MIX_SEQS / (32 * layer_us / 1e6), 1),
+            "decode_tokens_per_s_is": "2048 decode tokens per 32-layer step, the 32-layer step = 32 x the measured "
+                                      "layer-step",
+            "prefill_tokens_per_s": round(MIX_PROMPTS * MIX_PROMPT_LEN / (32 * layer_us / 1e6), 1),
+            "e2e": {"value": round(e2e_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / a.steps, 4), "rank": 0},
+            "roofline": roof.get("decode"), "write_roofline": roof.get("write"),
+            "clocks": clocks, "gpu_launches": a.steps * eng.launches_per_step(), "n_splits": eng.ns}), flush=True)
+    del graph, wgraph, dgraph, eng
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
