@@ -18,6 +18,7 @@ algorithmic bytes / its CUDA-event duration vs the measured HBM copy peak); the 
     python bench.py [--gpus N] [--steps K] [--warmup W]
     python bench.py --workload long           # BASELINE config 4 (kv heads partitioned over the GPUs)
     python bench.py --workload mix            # BASELINE config 5 (serving mix: prompt writes + ragged decode)
+    python bench.py --workload c1 | c2        # BASELINE configs 1 and 2 (single-layer Qwen2.5-7B geometry)
     python bench.py --impl reference          # the reference's CPU algorithm (C restatement) on the host cores
     torchrun --nproc-per-node N bench.py --gpus N ...
 """
@@ -331,9 +332,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["batch", "long", "mix"], default="batch",
+    ap.add_argument("--workload", choices=["batch", "long", "mix", "c1", "c2"], default="batch",
                     help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned); "
-                         "mix: config 5 (serving mix, requests partitioned)")
+                         "mix: config 5 (serving mix); c1, c2: configs 1 and 2 (single layer; requests partitioned)")
     a = ap.parse_args()
     if a.workload == "long":
         for k, v in (("batch", 4), ("context", 131072), ("page", 32), ("layers", 8)):
@@ -355,8 +356,10 @@ def main() -> None:
     if a.workload == "long":
         run_long(a, world, rank, local)
         return
-    if a.workload == "mix":
-        run_mix(a, world, rank, local)
+    if a.workload in ("mix", "c1", "c2"):
+        if a.workload == "c2" and a.steps == ap.get_default("steps"):
+            a.steps = 16                           # config 2: 16 consecutive steps timed
+        run_ragged(a, world, rank, local, a.workload)
         return
 
     torch.cuda.set_device(local)
@@ -559,7 +562,7 @@ def run_long(a, world: int, rank: int, local: int) -> None:
         dist.destroy_process_group()
 
 
-# ---------------------------------------------------------------- config 5: serving mix
+# ---------------------------------------------------------------- ragged workloads: BASELINE configs 1, 2 and 5
 MIX_SEQS, MIX_PROMPTS, MIX_PROMPT_LEN = 2048, 32, 2048
 
 
@@ -570,16 +573,58 @@ def mix_lengths(seed: int = 5) -> list[int]:
     return [int(min(16384, max(1, round(math.exp(v))))) for v in x.tolist()]
 
 
-class MixEngine:
-    """BASELINE config 5 state on one GPU for this rank's share of the requests: L layers of the decode sequences'
-    caches (ragged lengths) plus the pages of this rank's share of the 32 prompts, and the per-step inputs."""
+def offsets_qwen(hkv: int, D: int, gen: torch.Generator) -> torch.Tensor:
+    """Configs 1 and 2: per kv head 4 of the 128 key channels offset by +-20 (random sign), the rest by N(0, 0.5)."""
+    off = torch.randn(hkv, D, generator=gen) * 0.5
+    for h in range(hkv):
+        idx = torch.randperm(D, generator=gen)[:4]
+        off[h, idx] = 20 * torch.sign(torch.randn(4, generator=gen))
+    return off
 
-    def __init__(self, lens: list[int], n_prompts: int, L: int, device: torch.device, seed: int, extra_tokens: int):
+
+def offsets_llama(hkv: int, D: int, gen: torch.Generator) -> torch.Tensor:
+    """Configs 3 and 5: key offsets N(0, 2) plus 2 outlier channels at +-15 per kv head."""
+    off = torch.randn(hkv, D, generator=gen) * 2
+    for h in range(hkv):
+        idx = torch.randperm(D, generator=gen)[:2]
+        off[h, idx] = 15 * torch.sign(torch.randn(2, generator=gen))
+    return off
+
+
+def ragged_config(which: str, layers: int) -> dict:
+    """The shapes of BASELINE configs 1 (c1), 2 (c2) and 5 (mix)."""
+    if which == "c1":
+        return dict(name="BASELINE config 1: Qwen2.5-7B attention geometry (28 q / 4 kv heads, head_dim 128), int4, "
+                         "8 sequences x 2048 tokens written by quantize-on-write, page 32; one step = append + decode",
+                    model="Qwen2.5-7B (attention geometry only)", hq=28, hkv=4, bits=4, P=32, lens=[2048] * 8,
+                    prompts=0, layers=1, offsets=offsets_qwen, seed=0)
+    if which == "c2":
+        gen = torch.Generator().manual_seed(2)
+        lens = torch.randint(256, 8193, (64,), generator=gen).tolist()
+        return dict(name="BASELINE config 2: Qwen2.5-7B attention geometry, int8, 64 sequences with lengths "
+                         "U[256, 8192], page 32; one step = append one token per sequence + decode",
+                    model="Qwen2.5-7B (attention geometry only)", hq=28, hkv=4, bits=8, P=32, lens=lens, prompts=0,
+                    layers=1, offsets=offsets_qwen, seed=2)
+    return dict(name="BASELINE config 5: Llama-3.1-8B attention geometry, int4, page 16, 2048 sequences (lognormal "
+                     "lengths, median 2048, sigma 0.8, cap 16384) + per step 32 prompts of 2048 tokens; "
+                     f"{layers} of the 32 layers per step (all layers are the same work)",
+                model="Llama-3.1-8B (attention geometry only: 32 q heads, 8 kv heads, head_dim 128)", hq=32, hkv=8,
+                bits=4, P=16, lens=mix_lengths(), prompts=MIX_PROMPTS, layers=layers, offsets=offsets_llama, seed=5)
+
+
+class RaggedEngine:
+    """One GPU's share of a ragged workload: L layers of the decode sequences' caches, the pages of its share of the
+    per-step prompts (config 5), and the per-step inputs.  keep_fill keeps layer 0's context K/V (one ragged write
+    of every sequence) for the write roofline."""
+
+    def __init__(self, cfg: dict, lens: list[int], n_prompts: int, device: torch.device, seed: int,
+                 extra_tokens: int, keep_fill: bool):
         from kushkash_b200 import Ops
-        self.dev, self.L, self.lens, self.PR = device, L, lens, n_prompts
-        self.D, self.HKV, self.HQ, self.bits, self.P = 128, 8, 32, 4, 16
-        D, H, P = self.D, self.HKV, self.P
-        self.RB = 2 * P * (D // 2) + 4 * D + 4 * P
+        self.dev, self.L, self.lens, self.PR = device, cfg["layers"], lens, n_prompts
+        self.D, self.HKV, self.HQ, self.bits, self.P = 128, cfg["hkv"], cfg["hq"], cfg["bits"], cfg["P"]
+        D, H, P, L = self.D, self.HKV, self.P, self.L
+        self.DC = D // 2 if self.bits == 4 else D
+        self.RB = 2 * P * self.DC + 4 * D + 4 * P
         self.ops = Ops(device, D, self.bits, self.HQ // H, torch.bfloat16, P)
         S = self.S = len(lens)
         gen = torch.Generator().manual_seed(seed)
@@ -587,8 +632,7 @@ class MixEngine:
         ppr = MIX_PROMPT_LEN // P
         n_blocks = int(pages.sum()) + n_prompts * ppr
         perm = torch.randperm(n_blocks, generator=gen).to(torch.int32)
-        maxp = int(pages.max()) if S else 1
-        bt = torch.zeros(max(S, 1), maxp, dtype=torch.int32)
+        bt = torch.zeros(max(S, 1), int(pages.max()) if S else 1, dtype=torch.int32)
         o = 0
         for s, n in enumerate(pages.tolist()):
             bt[s, :n] = perm[o:o + n]
@@ -597,118 +641,233 @@ class MixEngine:
         self.bt_pr = perm[o:].view(n_prompts, ppr).to(device)
         self.pool = torch.zeros(L, n_blocks, H, self.RB, dtype=torch.uint8, device=device)
         self.tail_dec = torch.zeros(L, max(S, 1), H, P, D, dtype=torch.bfloat16, device=device)
-        self.tail_pr = torch.zeros(L, n_prompts, H, P, D, dtype=torch.bfloat16, device=device)
+        self.tail_pr = torch.zeros(L, max(n_prompts, 1), H, P, D, dtype=torch.bfloat16, device=device)
         self.ti_dec = torch.arange(max(S, 1), dtype=torch.int32, device=device)
-        self.ti_pr = torch.arange(n_prompts, dtype=torch.int32, device=device)
+        self.ti_pr = torch.arange(max(n_prompts, 1), dtype=torch.int32, device=device)
         self.sl_dec = torch.zeros(L, max(S, 1), dtype=torch.int32, device=device)
-        self.sl_pr = torch.full((n_prompts,), MIX_PROMPT_LEN, dtype=torch.int32, device=device)
-        self.offsets = (torch.randn(H, D, generator=gen) * 2).to(device)
-        for h in range(H):
-            idx = torch.randperm(D, generator=gen)[:2]
-            self.offsets[h, idx] = (15 * torch.sign(torch.randn(2, generator=gen))).to(device)
+        self.sl_pr = torch.full((max(n_prompts, 1),), MIX_PROMPT_LEN, dtype=torch.int32, device=device)
+        self.offsets = cfg["offsets"](H, D, gen).to(device)
         self.scale = 1.0 / math.sqrt(D)
         self.ns = self.ops.splits(S, H, max(lens) // P) if S else 1
         self.work = torch.empty(max(1, self.ops.work_size(max(S, 1), H, self.ns)), device=device)
         dgen = torch.Generator(device=device).manual_seed(seed + 1)
-        self._fill(dgen)
-        # per-step inputs: the prompts' K/V per layer, one new token per decode sequence and layer, q; outputs
+        self.fill_in = None
+        self._fill(dgen, keep_fill)
+        self.sl_init = self.sl_dec.clone()
         T = n_prompts * MIX_PROMPT_LEN
-        self.pk = (torch.randn(L, T, H, D, generator=dgen, device=device) + self.offsets).to(torch.bfloat16)
-        self.pv = torch.randn(L, T, H, D, generator=dgen, device=device).to(torch.bfloat16)
-        self.pqsl = torch.arange(n_prompts + 1, dtype=torch.int32, device=device) * MIX_PROMPT_LEN
-        self.pjs = torch.arange(n_prompts, dtype=torch.int32, device=device).repeat_interleave(ppr)
-        self.pjp = torch.arange(ppr, dtype=torch.int32, device=device).repeat(n_prompts)
+        if n_prompts:
+            self.pk = (torch.randn(L, T, H, D, generator=dgen, device=device) + self.offsets).to(torch.bfloat16)
+            self.pv = torch.randn(L, T, H, D, generator=dgen, device=device).to(torch.bfloat16)
+            self.pqsl = torch.arange(n_prompts + 1, dtype=torch.int32, device=device) * MIX_PROMPT_LEN
+            self.pjs = torch.arange(n_prompts, dtype=torch.int32, device=device).repeat_interleave(ppr)
+            self.pjp = torch.arange(ppr, dtype=torch.int32, device=device).repeat(n_prompts)
         self.k_new = (torch.randn(L, max(S, 1), H, D, generator=dgen, device=device) + self.offsets).to(torch.bfloat16)
         self.v_new = torch.randn(L, max(S, 1), H, D, generator=dgen, device=device).to(torch.bfloat16)
         self.q = torch.randn(L, max(S, 1), self.HQ, D, generator=dgen, device=device).to(torch.bfloat16)
         self.out = torch.empty_like(self.q)
 
-    def _fill(self, dgen) -> None:
-        """Bulk quantize-on-write of every decode sequence's context, per layer, in ragged chunks of <= 256k tokens."""
-        D, H, P, dev = self.D, self.HKV, self.P, self.dev
+    def _jobs(self, seqs: list[int]):
+        """Ragged write arguments for the whole contexts of `seqs`: query_start_loc over all S, job (seq, page)."""
         lens = torch.tensor(self.lens, dtype=torch.int64)
+        rows = torch.zeros(self.S, dtype=torch.int64)
+        rows[seqs] = lens[seqs]
+        qsl = torch.cat([torch.zeros(1, dtype=torch.int64), rows.cumsum(0)]).to(torch.int32)
+        npg = -(-lens[seqs] // self.P)
+        js = torch.tensor(seqs, dtype=torch.int64).repeat_interleave(npg)
+        start = torch.cat([torch.zeros(1, dtype=torch.int64), npg.cumsum(0)[:-1]]).repeat_interleave(npg)
+        jp = torch.arange(int(npg.sum())) - start
+        d = self.dev
+        return qsl.to(d), js.to(torch.int32).to(d), jp.to(torch.int32).to(d), int(rows.sum())
+
+    def _fill(self, dgen, keep: bool) -> None:
+        """Bulk quantize-on-write of every decode sequence's context, per layer, in ragged chunks (one chunk when the
+        inputs are kept)."""
+        D, H = self.D, self.HKV
+        limit = 1 << 62 if keep else 262144
         chunks, cur, tok = [], [], 0
         for s, n in enumerate(self.lens):
-            if cur and tok + n > 262144:
+            if cur and tok + n > limit:
                 chunks.append(cur)
                 cur, tok = [], 0
             cur.append(s)
             tok += n
         if cur:
             chunks.append(cur)
+        lens = torch.tensor(self.lens, dtype=torch.int32)
         for layer in range(self.L):
             for ch in chunks:
-                rows = torch.zeros(self.S, dtype=torch.int64)
-                rows[ch] = lens[ch]
-                qsl = torch.cat([torch.zeros(1, dtype=torch.int64), rows.cumsum(0)]).to(torch.int32).to(dev)
-                npg = -(-lens[ch] // P)
-                js = torch.tensor(ch, dtype=torch.int64).repeat_interleave(npg)
-                start = torch.cat([torch.zeros(1, dtype=torch.int64), npg.cumsum(0)[:-1]]).repeat_interleave(npg)
-                jp = torch.arange(int(npg.sum())) - start
-                T = int(rows.sum())
-                k = (torch.randn(T, H, D, generator=dgen, device=dev) + self.offsets).to(torch.bfloat16)
-                v = torch.randn(T, H, D, generator=dgen, device=dev).to(torch.bfloat16)
-                self.sl_dec[layer, ch] = lens[ch].to(torch.int32).to(dev)
-                self.ops.write(k, v, qsl, self.sl_dec[layer], self.ti_dec, js.to(torch.int32).to(dev),
-                               jp.to(torch.int32).to(dev), self.pool[layer], self.bt_dec, self.tail_dec[layer])
-        torch.cuda.synchronize(dev)
+                qsl, js, jp, T = self._jobs(ch)
+                k = (torch.randn(T, H, D, generator=dgen, device=self.dev) + self.offsets).to(torch.bfloat16)
+                v = torch.randn(T, H, D, generator=dgen, device=self.dev).to(torch.bfloat16)
+                self.sl_dec[layer, ch] = lens[ch].to(self.dev)
+                self.ops.write(k, v, qsl, self.sl_dec[layer], self.ti_dec, js, jp, self.pool[layer], self.bt_dec,
+                               self.tail_dec[layer])
+                if keep and layer == 0:
+                    self.fill_in = (k, v, qsl, js, jp)
+        torch.cuda.synchronize(self.dev)
+
+    def rewrite(self) -> None:
+        """Layer 0's whole contexts again (the kept fill inputs), from the initial lengths."""
+        k, v, qsl, js, jp = self.fill_in
+        self.sl_dec[0].copy_(self.sl_init[0])
+        self.ops.write(k, v, qsl, self.sl_dec[0], self.ti_dec, js, jp, self.pool[0], self.bt_dec, self.tail_dec[0])
 
     def prefill(self, layer: int) -> None:
         self.ops.write(self.pk[layer], self.pv[layer], self.pqsl, self.sl_pr, self.ti_pr, self.pjs, self.pjp,
                        self.pool[layer], self.bt_pr, self.tail_pr[layer])
 
-    def decode_step(self, layer: int) -> None:
-        self.ops.append(self.k_new[layer], self.v_new[layer], self.sl_dec[layer], self.ti_dec, self.pool[layer],
-                        self.bt_dec, self.tail_dec[layer], pos_offset=0, advance=True)
+    def decode(self, layer: int) -> None:
         self.ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.bt_dec, self.sl_dec[layer], self.ti_dec,
                         self.tail_dec[layer], self.scale, self.ns, self.work)
 
     def step(self) -> None:
-        """One step of every layer: bulk prefill-quantize of the prompts, append + decode of every sequence."""
+        """One step of every layer: the prompts' bulk prefill-quantize (config 5), append + decode of every sequence."""
         for layer in range(self.L):
-            self.prefill(layer)
+            if self.PR:
+                self.prefill(layer)
             if self.S:
-                self.decode_step(layer)
+                self.ops.append(self.k_new[layer], self.v_new[layer], self.sl_dec[layer], self.ti_dec,
+                                self.pool[layer], self.bt_dec, self.tail_dec[layer], pos_offset=0, advance=True)
+                self.decode(layer)
 
-    def decode_bytes(self, extra: int) -> int:
+    def decode_bytes(self, extra: int, seqs: list[int] | None = None) -> int:
         """Packed-KV bytes of one decode layer-step with every sequence `extra` tokens past its initial length."""
-        full, tot = 0, 0
-        for n in self.lens:
+        tot = 0
+        for n in (self.lens if seqs is None else [self.lens[i] for i in seqs]):
             f, r = divmod(n + extra, self.P)
-            tot += f * self.RB + r * (2 * self.D + self.D // 2 + 4)
+            tot += f * self.RB + r * (2 * self.D + self.DC + 4)
         return tot * self.HKV
 
+    def io_bytes(self) -> int:
+        """q in and out of one decode layer-step (bf16)."""
+        return self.S * self.HQ * self.D * 4
+
     def prefill_bytes(self) -> int:
-        """Algorithmic bytes of one prompt write: bf16 K and V in, records out."""
+        """Algorithmic bytes of one layer's prompt write: bf16 K and V in, records out."""
         T = self.PR * MIX_PROMPT_LEN
         return 2 * T * self.HKV * self.D * 2 + (T // self.P) * self.HKV * self.RB
 
+    def fill_bytes(self) -> int:
+        """Algorithmic bytes of layer 0's whole-context write: bf16 K and V in, records (and partial pages' V rows
+        and tail K rows) out."""
+        T = sum(self.lens)
+        return 2 * T * self.HKV * self.D * 2 + self.decode_bytes(0)
+
     def append_bytes(self) -> int:
         """Per layer: k, v rows in (bf16), the V code row and scale/bias and the exact K tail row out."""
-        return self.S * self.HKV * (4 * self.D + self.D // 2 + 4 + 2 * self.D)
+        return self.S * self.HKV * (4 * self.D + self.DC + 4 + 2 * self.D)
 
     def launches_per_step(self) -> int:
-        return self.L * (1 + (2 + (1 if self.ns > 1 else 0) if self.S else 0))
+        return self.L * ((1 if self.PR else 0) + ((2 + (1 if self.ns > 1 else 0)) if self.S else 0))
 
 
-def run_mix(a, world: int, rank: int, local: int) -> None:
-    """BASELINE config 5 (whole-box serving mix): 2048 concurrent sequences with lognormal context lengths and, per
-    step, a bulk prefill-quantize of 32 new 2048-token prompts plus a one-token append and attention for every
-    sequence; requests (sequences and prompts) are partitioned over the GPUs by tokens, no collective in the step.
-    32 layers of caches (~236 GB) do not fit one B200, so a step covers a subset of L layers (every layer is the same
-    work) and the 32-layer figures are the measured layer-step time x 32."""
+def time_graph(gr, dev, reps: int = 3) -> float:
+    """ms per replay of a captured graph (one untimed replay first), CUDA events on the capture stream."""
+    gr.replay()
+    torch.cuda.synchronize(dev)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for _ in range(reps):
+        gr.replay()
+    k1.record()
+    torch.cuda.synchronize(dev)
+    return k0.elapsed_time(k1) / reps
+
+
+def time_cpu_ragged(cfg: dict, seqs: list[int], n_prompts: int, budget_s: float) -> dict:
+    """The oracle on the host cores over a sample of a ragged workload (the given sequences at their lengths and
+    n_prompts prompts): layer-steps of prompt write + append + decode until budget_s."""
+    from oracle.kush_oracle import OracleOps, set_threads
+    cores = set_threads(0)
+    D, H, P, bits, hq = 128, cfg["hkv"], cfg["P"], cfg["bits"], cfg["hq"]
+    lens = [cfg["lens"][i] for i in seqs]
+    gen = torch.Generator().manual_seed(99)
+    off = cfg["offsets"](H, D, gen)
+    ops = OracleOps(D, bits, hq // H, P)
+    dc = D // 2 if bits == 4 else D
+    rb = 2 * P * dc + 4 * D + 4 * P
+    S = len(lens)
+    max_iters = 2000                                    # every iteration appends one token per sequence: room for all
+    pages = [-(-(n + max_iters + 8) // P) for n in lens]
+    ppr = MIX_PROMPT_LEN // P
+    nb = sum(pages) + n_prompts * ppr
+    pool = torch.zeros(nb, H, rb, dtype=torch.uint8)
+    perm = torch.randperm(nb, generator=gen).to(torch.int32)
+    bt = torch.zeros(S, max(pages), dtype=torch.int32)
+    o = 0
+    for s, n in enumerate(pages):
+        bt[s, :n] = perm[o:o + n]
+        o += n
+    bt_pr = perm[o:].view(n_prompts, ppr) if n_prompts else None
+    tail = torch.zeros(S, H, P, D)
+    ti = torch.arange(S, dtype=torch.int32)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    T = sum(lens)
+    k = (torch.randn(T, H, D, generator=gen) + off).bfloat16().float()
+    v = torch.randn(T, H, D, generator=gen).bfloat16().float()
+    qsl = torch.cat([torch.zeros(1, dtype=torch.int64), torch.tensor(lens).cumsum(0)]).to(torch.int32)
+    npg = [-(-n // P) for n in lens]
+    js = torch.tensor([s for s in range(S) for _ in range(npg[s])], dtype=torch.int32)
+    jp = torch.tensor([p for s in range(S) for p in range(npg[s])], dtype=torch.int32)
+    ops.write(k, v, qsl, sl, ti, js, jp, pool, bt, tail)
+    q = torch.randn(S, hq, D, generator=gen).bfloat16().float()
+    kn = (torch.randn(S, H, D, generator=gen) + off).bfloat16().float()
+    vn = torch.randn(S, H, D, generator=gen).bfloat16().float()
+    out = torch.empty_like(q)
+    if n_prompts:
+        pk = (torch.randn(n_prompts * MIX_PROMPT_LEN, H, D, generator=gen) + off).bfloat16().float()
+        pv = torch.randn(n_prompts * MIX_PROMPT_LEN, H, D, generator=gen).bfloat16().float()
+        pqsl = torch.arange(n_prompts + 1, dtype=torch.int32) * MIX_PROMPT_LEN
+        psl = torch.full((n_prompts,), MIX_PROMPT_LEN, dtype=torch.int32)
+        pti = torch.arange(n_prompts, dtype=torch.int32)
+        ptail = torch.zeros(n_prompts, H, P, D)
+        pjs = torch.arange(n_prompts, dtype=torch.int32).repeat_interleave(ppr)
+        pjp = torch.arange(ppr, dtype=torch.int32).repeat(n_prompts)
+    iters, byts, t0 = 0, 0, time.perf_counter()
+    while True:
+        if n_prompts:
+            ops.write(pk, pv, pqsl, psl, pti, pjs, pjp, pool, bt_pr, ptail)
+            byts += 2 * pk.numel() * 2 + (pk.shape[0] // P) * H * rb
+        ops.append(kn, vn, sl, ti, pool, bt, tail, pos_offset=0, advance=True)
+        ops.decode(q, out, pool, bt, sl, ti, tail, 1.0 / math.sqrt(D))
+        byts += S * H * (4 * D + dc + 4 + 2 * D)
+        for n in sl.tolist():
+            f, r = divmod(n, P)
+            byts += H * (f * rb + r * (2 * D + dc + 4))
+        iters += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or iters >= max_iters:
+            break
+    return {"value": round(byts / el / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{iters} layer-steps ({'prompt write + ' if n_prompts else ''}append + decode) of {S} of the "
+                      f"{len(cfg['lens'])} sequences{f' and {n_prompts} of the prompts' if n_prompts else ''}, "
+                      f"{el:.1f} s"}
+
+
+def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
+    """BASELINE configs 1 (c1), 2 (c2) and 5 (mix): ragged decode sequences (and, for config 5, per-step prompt bulk
+    writes) with requests partitioned over the GPUs by tokens, no collective in the step.  Config 5's 32 layers of
+    caches (~236 GB) do not fit one B200, so its step covers a subset of the layers (every layer is the same work)
+    and its 32-layer figures are the measured layer-step time x 32."""
     from kushkash_b200.shard import partition_requests
+    cfg = ragged_config(which, a.layers)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    lens_all = mix_lengths()
+    lens_all = cfg["lens"]
     mine = partition_requests(lens_all, world)[rank]
     lens = [lens_all[i] for i in mine]
-    n_pr = MIX_PROMPTS // world
-    eng = MixEngine(lens, n_pr, a.layers, dev, seed=777 + rank, extra_tokens=a.warmup + 2 * a.steps + 8)
+    n_pr = cfg["prompts"] // world
+    eng = RaggedEngine(cfg, lens, n_pr, dev, seed=cfg["seed"] * 100 + rank, extra_tokens=a.warmup + 2 * a.steps + 8,
+                       keep_fill=n_pr == 0)
+    kern = {}
+    if n_pr == 0:                                   # write roofline: layer 0's whole contexts again
+        wgraph = capture(eng.rewrite, dev)
+        kern["write"] = (eng.fill_bytes(), time_graph(wgraph, dev))
+        del wgraph
 
     def barrier():
         if dist is not None:
@@ -730,28 +889,24 @@ def run_mix(a, world: int, rank: int, local: int) -> None:
     clocks = sampler.stop()
     barrier()
     ms = e0.elapsed_time(e1)
-    byts = sum(eng.decode_bytes(n_done + i + 1) for i in range(a.steps)) if eng.S else 0
-    byts = (byts + a.steps * (eng.prefill_bytes() + eng.append_bytes())) * eng.L
+
+    def step_bytes(first: int) -> int:
+        b = sum(eng.decode_bytes(first + i + 1) for i in range(a.steps)) if eng.S else 0
+        return (b + a.steps * (eng.prefill_bytes() * (1 if eng.PR else 0) + eng.append_bytes())) * eng.L
+
+    byts = step_bytes(n_done)
     n_done += a.steps
-    # per-kernel rooflines on this rank: prompt writes alone, decodes alone (graphs, CUDA events)
-    wgraph = capture(lambda: [eng.prefill(l) for l in range(eng.L)], dev)
-    dgraph = capture(lambda: [eng.ops.decode(eng.q[l], eng.out[l], eng.pool[l], eng.bt_dec, eng.sl_dec[l], eng.ti_dec,
-                                             eng.tail_dec[l], eng.scale, eng.ns, eng.work) for l in range(eng.L)], dev)
-    kern = {}
-    for name, gr, nbytes in (("write", wgraph, eng.prefill_bytes()), ("decode", dgraph, eng.decode_bytes(n_done)
-                                                                       + eng.S * eng.HQ * eng.D * 4)):
-        gr.replay()
-        torch.cuda.synchronize(dev)
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record()
-        for _ in range(3):
-            gr.replay()
-        k1.record()
-        torch.cuda.synchronize(dev)
-        kms = k0.elapsed_time(k1) / (3 * eng.L)
-        kern[name] = (nbytes, kms)
+    if eng.PR:
+        wgraph = capture(lambda: [eng.prefill(l) for l in range(eng.L)], dev)
+        kern["write"] = (eng.prefill_bytes(), time_graph(wgraph, dev) / eng.L)
+        del wgraph
+    if eng.S:
+        dgraph = capture(lambda: [eng.decode(l) for l in range(eng.L)], dev)
+        kern["decode"] = (eng.decode_bytes(n_done) + eng.io_bytes(), time_graph(dgraph, dev) / eng.L)
+        del dgraph
     # e2e: every step's inputs (prompt K/V, new tokens, q) from pinned host memory, outputs back
-    hin = {k: getattr(eng, k).cpu().pin_memory() for k in ("pk", "pv", "k_new", "v_new", "q")}
+    names = (("pk", "pv") if eng.PR else ()) + ("k_new", "v_new", "q")
+    hin = {k: getattr(eng, k).cpu().pin_memory() for k in names}
     hout = torch.empty(eng.out.shape, dtype=eng.out.dtype).pin_memory()
     barrier()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -765,8 +920,7 @@ def run_mix(a, world: int, rank: int, local: int) -> None:
     torch.cuda.synchronize(dev)
     barrier()
     e2e_ms = x0.elapsed_time(x1)
-    e2e_bytes = (sum(eng.decode_bytes(n_done + i + 1) for i in range(a.steps)) if eng.S else 0)
-    e2e_bytes = (e2e_bytes + a.steps * (eng.prefill_bytes() + eng.append_bytes())) * eng.L
+    e2e_bytes = step_bytes(n_done)
     h2d = sum(t.numel() * t.element_size() for t in hin.values())
     d2h = hout.numel() * hout.element_size()
     if dist is not None:
@@ -776,6 +930,10 @@ def run_mix(a, world: int, rank: int, local: int) -> None:
         b = torch.tensor([float(byts), float(e2e_bytes)], device=dev, dtype=torch.float64)
         dist.all_reduce(b)
         byts, e2e_bytes = (float(x) for x in b.tolist())
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        sample = list(range(len(lens_all))) if which != "mix" else list(range(16))
+        cpu = time_cpu_ragged(cfg, sample, 1 if cfg["prompts"] else 0, a.cpu_seconds)
     if rank == 0:
         peak, peak_kind = hbm_peak()
         ms_step = ms / a.steps
@@ -787,34 +945,40 @@ def run_mix(a, world: int, rank: int, local: int) -> None:
             roof[name] = {"kernel": f"kush_sm100_{name}", "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
                           "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
                           "algorithmic_bytes_per_launch": nb, "us_per_launch": round(kms * 1e3, 2), "rank": 0}
-        print(json.dumps({
+        S_all = len(lens_all)
+        line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
-            "data": "synthetic (seeded bf16 N(0,1) K/V/q, key offsets N(0, 2) + 2 outlier channels at +-15, lognormal "
-                    "lengths; BASELINE config 5 shapes)",
-            "config": {"workload": "BASELINE config 5: Llama-3.1-8B attention geometry, int4, page 16, 2048 sequences "
-                                   "(lognormal lengths, median 2048, sigma 0.8, cap 16384) + per step 32 prompts of "
-                                   f"2048 tokens; {eng.L} of the 32 layers per step (all layers are the same work)",
-                       "model": "Llama-3.1-8B (attention geometry only: 32 q heads, 8 kv heads, head_dim 128)",
-                       "global_batch": MIX_SEQS, "prompts_per_step": MIX_PROMPTS, "prompt_len": MIX_PROMPT_LEN,
-                       "cached_tokens": sum(lens_all), "layers_timed": eng.L, "page": 16, "bits": 4,
+            "vs_baseline": None, "dtype": f"int{cfg['bits']} records, bf16 q/k/v, fp32 softmax",
+            "data": f"synthetic (seeded bf16 N(0,1) K/V/q with per-channel key offsets; {cfg['name'].split(':')[0]} "
+                    "shapes)",
+            "config": {"workload": cfg["name"], "model": cfg["model"], "global_batch": S_all,
+                       "cached_tokens": sum(lens_all), "layers_timed": eng.L, "page": cfg["P"], "bits": cfg["bits"],
+                       "q_heads": cfg["hq"], "kv_heads": cfg["hkv"], "head_dim": 128,
                        "parallelism": f"requests partitioned over {world} GPU(s) by tokens, no collective in the step",
-                       "l2": "inputs larger than L2 (GBs of records per layer-step, no flush needed)"},
-            "value_is": "all bytes of the step (decode packed-KV reads + prompt bf16 in / records out + appends) over "
-                        "the max-over-ranks device time",
+                       "l2": ("inputs larger than L2 (GBs of records per layer-step, no flush needed)" if which == "mix"
+                              else "inputs smaller than L2: the graph replays re-read L2-resident records (launch- "
+                                   "and latency-bound sizes, as the config intends)")},
+            "value_is": "all bytes of the step (decode packed-KV reads + appends" +
+                        (" + prompt bf16 in / records out" if cfg["prompts"] else "") +
+                        ") over the max-over-ranks device time",
             "per_gpu_gbs": round(value / world, 1),
             "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "us_per_layer_step": round(layer_us, 2),
-            "decode_tokens_per_s": round(MIX_SEQS / (32 * layer_us / 1e6), 1),
-            "decode_tokens_per_s_is": "2048 decode tokens per 32-layer step, the 32-layer step = 32 x the measured "
-                                      "layer-step",
-            "prefill_tokens_per_s": round(MIX_PROMPTS * MIX_PROMPT_LEN / (32 * layer_us / 1e6), 1),
             "e2e": {"value": round(e2e_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / a.steps, 4), "rank": 0},
-            "roofline": roof.get("decode"), "write_roofline": roof.get("write"),
-            "clocks": clocks, "gpu_launches": a.steps * eng.launches_per_step(), "n_splits": eng.ns}), flush=True)
-    del graph, wgraph, dgraph, eng
+            "roofline": roof.get("decode"), "write_roofline": roof.get("write"), "cpu_baseline": cpu,
+            "clocks": clocks, "gpu_launches": a.steps * eng.launches_per_step(), "n_splits": eng.ns}
+        if which == "mix":
+            line["decode_tokens_per_s"] = round(S_all / (32 * layer_us / 1e6), 1)
+            line["decode_tokens_per_s_is"] = ("2048 decode tokens per 32-layer step, the 32-layer step = 32 x the "
+                                              "measured layer-step")
+            line["prefill_tokens_per_s"] = round(MIX_PROMPTS * MIX_PROMPT_LEN / (32 * layer_us / 1e6), 1)
+        else:
+            line["decode_tokens_per_s"] = round(S_all / (ms_step / 1e3), 1)
+            line["decode_tokens_per_s_is"] = "one layer (the config is a single-layer attention step)"
+        print(json.dumps(line), flush=True)
+    del graph, eng
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
