@@ -20,7 +20,9 @@
 //        S^T accumulators become P' B fragments with one movmatrix.trans per 8x8 block.
 // Codes become exact fp16 with the magic-number trick (a code under the exponent of 1024, then one subtract);
 // the D dimension is permuted so every lane's fragments come from whole 32-bit words of its token rows.
+#include <cuda.h>
 #include <stdio.h>
+#include <string.h>
 
 #include "kush_async.cuh"
 #include "kush_common.cuh"
@@ -69,15 +71,52 @@ __device__ __forceinline__ float fast_exp2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
-// lane 0 of the warp (predicated, no branch): arm `bar` for `bytes` and start one 1-D bulk copy src -> dst (shared
-// addresses).  The slot's previous contents were read into registers and consumed by MMAs before this point in
-// program order, so no proxy fence is needed between those reads and the async-proxy write.
+// int8 pages (rows of 128 bytes: the 8 token rows an ldmatrix reads would share their banks 8 ways) keep their K and
+// V code rows in shared memory XOR-swizzled in 16-byte chunks (TMA SWIZZLE_32B / 64B / 128B: chunk bits [4, 4 + b)
+// ^= address bits [7, 7 + b), m = 2^b - 1), so those rows, and the rows of a k-fragment load, fall in distinct
+// banks; m = 0 is the unswizzled layout.  Every region base is a multiple of the swizzle's 1024-byte period.  int4
+// pages (64-byte rows, 4-way) measured faster as one contiguous 1-D copy per page without the swizzle.
+__device__ __forceinline__ uint32_t swz(uint32_t o, uint32_t m) { return o ^ (((o >> 7) & m) << 4); }
+
+// lane 0 (predicated): arm `bar` for `bytes`, bring a page's K code box and V code box (tensor copies of the 3-D
+// map [row bytes, rows of a block, blocks], coordinates (0, row, blk) and (0, row + vrows, blk)) and its scale bytes
+// (1-D copy) into shared memory.  No multicast.
+__device__ __forceinline__ void refill_tma_lane0(uint32_t lane, uint32_t bar, uint32_t dst_codes, uint32_t vbox,
+                                                 const CUtensorMap* map, int32_t row, int32_t vrows, int32_t blk,
+                                                 uint32_t dst_scales, const void* src_scales, uint32_t scale_bytes,
+                                                 uint32_t bytes) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.eq.u32 p, %0, 0;\n"
+        " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n"
+        " @p cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%3], [%4, {%5, %6, %7}], [%1];\n"
+        " @p cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%8], [%4, {%5, %9, %7}], [%1];\n"
+        " @p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%10], [%11], %12, [%1];\n}\n" ::"r"(lane),
+        "r"(bar), "r"(bytes), "r"(dst_codes), "l"(map), "r"(0), "r"(row), "r"(blk), "r"(dst_codes + vbox),
+        "r"(row + vrows), "r"(dst_scales), "l"(src_scales), "r"(scale_bytes)
+        : "memory");
+}
+
+// lane 0 (predicated): a page as one 1-D copy of its record (int4 slots)
 __device__ __forceinline__ void refill_lane0(uint32_t lane, uint32_t bar, uint32_t dst, const void* src, uint32_t bytes) {
     asm volatile(
         "{\n .reg .pred p;\n setp.eq.u32 p, %0, 0;\n"
         " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %3;\n"
         " @p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%2], [%4], %3, [%1];\n}\n" ::"r"(lane),
         "r"(bar), "r"(dst), "r"(bytes), "l"(src)
+        : "memory");
+}
+
+// lane 0 (predicated): a page as two 1-D copies (code rows, then scales) into split slots, for pools a tensor map
+// cannot describe
+__device__ __forceinline__ void refill_bulk_lane0(uint32_t lane, uint32_t bar, uint32_t dst_codes, const uint8_t* src,
+                                                  uint32_t code_bytes, uint32_t dst_scales, uint32_t scale_bytes) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.eq.u32 p, %0, 0;\n"
+        " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n"
+        " @p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%3], [%4], %5, [%1];\n"
+        " @p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%6], [%7], %8, [%1];\n}\n" ::"r"(lane),
+        "r"(bar), "r"(code_bytes + scale_bytes), "r"(dst_codes), "l"(src), "r"(code_bytes), "r"(dst_scales),
+        "l"(src + code_bytes), "r"(scale_bytes)
         : "memory");
 }
 
@@ -141,25 +180,25 @@ __device__ __forceinline__ void load_pairs(const uint8_t* arr, int tid, uint32_t
     }
 }
 
-// K' = c * ks + dkb of token rows g (row0) and g + 8 (row1) of a 16-token tile, straight into m16n8k16 A-fragment
-// order: a[kt] = {row g pair 2kt, row g+8 pair 2kt, row g pair 2kt+1, row g+8 pair 2kt+1} (pair order of Lay::kdim)
+// K' = c * ks + dkb of token rows g (r = 0) and g + 8 (r = 1) of a 16-token tile, straight into m16n8k16 A-fragment
+// order: a[kt] = {row g pair 2kt, row g+8 pair 2kt, row g pair 2kt+1, row g+8 pair 2kt+1} (pair order of Lay::kdim).
+// The lane's bytes of row r, chunk i are at codes + koff[r][i] (swizzled offsets).
 template <int D, int BITS>
-__device__ __forceinline__ void k_frags(const uint8_t* row0, const uint8_t* row1, const uint32_t (&ks)[2 * (D / 16)],
-                                        const uint32_t (&dkb)[2 * (D / 16)], uint32_t (&a)[D / 16][4]) {
+__device__ __forceinline__ void k_frags(const uint8_t* codes, const uint32_t (&koff)[2][(Lay<D, BITS>::CW + 3) / 4],
+                                        const uint32_t (&ks)[2 * (D / 16)], const uint32_t (&dkb)[2 * (D / 16)],
+                                        uint32_t (&a)[D / 16][4]) {
     using L = Lay<D, BITS>;
     uint32_t w[2][L::CW];
 #pragma unroll
     for (int r = 0; r < 2; r++) {
-        const uint8_t* row = r ? row1 : row0;
         if constexpr (L::CW % 4 != 0) {                        // D = 64 int4: 8 bytes per lane
-            const uint2 v = *reinterpret_cast<const uint2*>(row);
+            const uint2 v = *reinterpret_cast<const uint2*>(codes + koff[r][0]);
             w[r][0] = v.x;
             w[r][1] = v.y;
         } else {
-            const uint4* src = reinterpret_cast<const uint4*>(row);
 #pragma unroll
             for (int i = 0; i < L::CW / 4; i++) {
-                const uint4 v = src[i];
+                const uint4 v = *reinterpret_cast<const uint4*>(codes + koff[r][i]);
                 w[r][4 * i] = v.x;
                 w[r][4 * i + 1] = v.y;
                 w[r][4 * i + 2] = v.z;
@@ -208,16 +247,16 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
 //   int4: chunk k, byte b gives m-tile 2k + b: row g = low nibbles (dim 16k + 2g + b), row g+8 = high nibbles
 //   int8: chunk k gives m-tile k: row g = byte 2g (dim 16k + 2g), row g+8 = byte 2g+1
 // a[mt] = {row g x tokens 2tid,2tid+1 | row g+8 x same | row g x tokens 2tid+8,+9 | row g+8 x same}, exact codes.
+// voff[ld]: this lane's (swizzled) row address offset of load ld -- matrices (tokens 0-7, chunk 2ld), (0-7, 2ld+1),
+// (8-15, 2ld), (8-15, 2ld+1), lane (mi, rr) addressing row rr of matrix mi.
 template <int D, int BITS>
-__device__ __forceinline__ void v_frags(uint32_t vq, int lane, uint32_t (&a)[D / 16][4]) {
+__device__ __forceinline__ void v_frags(uint32_t vq, const uint32_t (&voff)[Lay<D, BITS>::DC / 32], uint32_t (&a)[D / 16][4]) {
     using L = Lay<D, BITS>;
     constexpr int NCH = L::DC / 16;                       // 16-byte chunks per token row
-    const int mi = lane >> 3, rr = lane & 7;               // this lane addresses row rr of matrix mi of each load
 #pragma unroll
     for (int ld = 0; ld < NCH / 2; ld++) {
-        // matrices of load ld: (tokens 0-7, chunk 2ld), (0-7, 2ld+1), (8-15, 2ld), (8-15, 2ld+1)
         uint32_t r[4];
-        ldsm_x4_trans(vq + ((mi >> 1) * 8 + rr) * L::DC + 16 * (2 * ld + (mi & 1)), r);
+        ldsm_x4_trans(vq + voff[ld], r);
 #pragma unroll
         for (int c = 0; c < 2; c++) {                     // chunk k = 2 ld + c
             const int k = 2 * ld + c;
@@ -246,14 +285,22 @@ __device__ __forceinline__ void v_frags(uint32_t vq, int lane, uint32_t (&a)[D /
 template <int D, int BITS, int P, int NT>
 struct MmaCfg {
     static constexpr int RB = Fmt<D, BITS, P>::RB;
+    static constexpr int CODES = 2 * P * Fmt<D, BITS, P>::DC;     // K then V code rows of a page
+    static constexpr int SCALES = RB - CODES;                      // ks, kb, vs, vb
+    // int8: split slots (code rows, swizzled by tensor copies, apart from the scales); int4: one record per slot
+    static constexpr bool SPLIT = BITS == 8;
+    static constexpr int CSTRIDE = SPLIT ? CODES : RB;             // code slot stride
     // ring slots per warp: deep enough to keep ~2 pages in flight per warp at 4 CTAs per SM
     static constexpr int NS = RB <= 3072 ? 4 : 2;
     static constexpr int GMAX = 8 * NT;
     static constexpr int MERGE = 4 * ((MMA_NW + 1) * GMAX * D + 2 * (MMA_NW + 1) * GMAX);
     static constexpr int RING = MMA_NW * NS * RB > MERGE ? MMA_NW * NS * RB : (MERGE + 127) / 128 * 128;
     static constexpr int BARS = (8 * MMA_NW * NS + 127) / 128 * 128;
-    // shared memory: [bars | ring (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D])]
-    static constexpr int SMEM = BARS + RING + 4 * (GMAX * D + D);
+    // shared memory: [bars | pad to 1024 | ring: int8 code slots [NW][NS][CODES] + scale slots [NW][NS][SCALES], int4
+    // record slots [NW][NS][RB] (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D])]; the pad aligns
+    // the code slots to the swizzle period
+    static constexpr int SMEM = 1024 + BARS + RING + 4 * (GMAX * D + D);
+    static_assert(!SPLIT || (CODES % 1024 == 0 && SCALES % 16 == 0), "code slots must keep the swizzle period");
     // CTAs per SM the register budget targets (the larger tiles need more registers per thread)
     static constexpr int MINB = (D == 64 || (D == 128 && NT == 1 && !(BITS == 8 && P == 32))) ? 4
                                 : NT == 1 && D == 128 ? 3 : 2;
@@ -269,14 +316,16 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
-    float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o) {
+    float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o,
+    const __grid_constant__ CUtensorMap tmap, int use_tma, uint32_t swz_m, int32_t rows_per_head, int32_t box_rows) {
     using F = Fmt<D, BITS, P>;
     using L = Lay<D, BITS>;
     using C = MmaCfg<D, BITS, P, NT>;
     constexpr int NW = MMA_NW, NS = C::NS, KT = L::KT, MT = L::MT, MTT = P / 16;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // [NW][NS]
-    uint8_t* ring = smem + C::BARS;                                     // [NW][NS][RB], reused for the merge
+    const uint32_t smem0 = smem_u32(smem);
+    uint8_t* ring = smem + (((smem0 + C::BARS + 1023u) & ~1023u) - smem0);   // code + scale slots, reused by the merge
     float* qsm = reinterpret_cast<float*>(ring + C::RING);              // [G][D] q * scale * log2e
     float* kbr = qsm + G * D;                                           // [D] kb_ref
     const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
@@ -297,16 +346,36 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     // my pages: p0 + wid + i * NW, i < npw; start their copies before anything else
     const int64_t mine0 = p0 + wid;
     const int npw = mine0 < p1 ? int((p1 - mine0 + NW - 1) / NW) : 0;
-    uint8_t* wring = ring + wid * NS * C::RB;
+    uint8_t* wcodes = ring + wid * NS * C::CSTRIDE;                     // this warp's code (int4: record) slots
+    uint8_t* wscl = ring + NW * NS * C::CODES + wid * NS * C::SCALES;   // and its scale slots (int8)
     uint64_t* wbar = bars + wid * NS;
     auto bt_at = [&](int i) -> int32_t { return i < npw ? bt[mine0 + int64_t(i) * NW] : 0; };
     int32_t btw = bt_at(lane), btn = bt_at(32 + lane);                 // block ids of my pages, 32 at a time
-    const uint32_t ring_u = smem_u32(wring), bar_u = smem_u32(wbar);
+    const uint32_t codes_u = smem_u32(wcodes), scl_u = smem_u32(wscl), bar_u = smem_u32(wbar);
+    const int32_t hrow = h * rows_per_head;                             // the record's first row in the tensor map
     auto issue = [&](int i, int32_t blk) {                              // lane 0: page i -> slot i % NS
         const uint32_t slot = uint32_t(i) % NS;
-        refill_lane0(uint32_t(lane), bar_u + 8 * slot, ring_u + slot * C::RB, hcache + int64_t(blk) * block_stride,
-                     C::RB);
+        const uint8_t* src = hcache + int64_t(blk) * block_stride;
+        if constexpr (!C::SPLIT)
+            refill_lane0(uint32_t(lane), bar_u + 8 * slot, codes_u + slot * C::RB, src, C::RB);
+        else if (use_tma)
+            refill_tma_lane0(uint32_t(lane), bar_u + 8 * slot, codes_u + slot * C::CODES, C::CODES / 2, &tmap, hrow,
+                             box_rows, blk, scl_u + slot * C::SCALES, src + C::CODES, C::SCALES, C::RB);
+        else
+            refill_bulk_lane0(uint32_t(lane), bar_u + 8 * slot, codes_u + slot * C::CODES, src, C::CODES,
+                              scl_u + slot * C::SCALES, C::SCALES);
     };
+    // this lane's swizzled offsets in a 16-token tile: K rows g, g + 8 at its bytes; V ldmatrix row addresses
+    // (a tile 16 rows further keeps the same swizzle: 16 rows move the row bits by a multiple of the period)
+    const uint32_t sm = C::SPLIT ? swz_m : 0u;                         // int4: a constant 0 (offsets fold away)
+    uint32_t koff[2][(L::CW + 3) / 4], voff[L::DC / 32];
+#pragma unroll
+    for (int r = 0; r < 2; r++)
+#pragma unroll
+        for (int i = 0; i < (L::CW + 3) / 4; i++) koff[r][i] = swz(uint32_t((g + 8 * r) * F::DC + tid * L::CB + 16 * i), sm);
+#pragma unroll
+    for (int ld = 0; ld < L::DC / 32; ld++)
+        voff[ld] = swz(uint32_t((((lane >> 3) >> 1) * 8 + (lane & 7)) * F::DC + 16 * (2 * ld + ((lane >> 3) & 1))), sm);
     __syncthreads();                                                    // barriers initialised
 #pragma unroll 1
     for (int i = 0; i < NS && i < npw; i++) issue(i, __shfl_sync(0xffffffffu, btw, i));
@@ -358,7 +427,8 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             fail_at = i;
             break;
         }
-        const uint8_t* rec = wring + slot * C::RB;
+        const uint8_t* codes = wcodes + slot * C::CSTRIDE;               // K rows, then V rows (int8: swizzled)
+        const uint8_t* scl = C::SPLIT ? wscl + slot * C::SCALES : codes + C::CODES;   // ks, kb, vs, vb
         // one 16-token tile at a time (P = 32 pages have two): QK, online softmax, PV.  The softmax is tile-granular,
         // which keeps the register footprint of both page sizes the same.
 #pragma unroll
@@ -368,13 +438,12 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
                 // the page's K scale and bias pairs for this lane's dims (K' = c * ks + (kb - kb_ref)); reloaded per
                 // tile rather than held across the tiles of a 32-token page (register pressure)
                 uint32_t ks[2 * KT], dkb[2 * KT];
-                load_pairs<D, BITS>(rec + F::OFF_KS, tid, ks);
-                load_pairs<D, BITS>(rec + F::OFF_KB, tid, dkb);
+                load_pairs<D, BITS>(scl, tid, ks);
+                load_pairs<D, BITS>(scl + 2 * D, tid, dkb);
 #pragma unroll
                 for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref[e]);
                 uint32_t ka[KT][4];                                       // A fragments of this 16-token tile
-                const uint8_t* r0 = rec + (mtt * 16 + g) * F::DC + tid * L::CB;
-                k_frags<D, BITS>(r0, r0 + 8 * F::DC, ks, dkb, ka);
+                k_frags<D, BITS>(codes + mtt * 16 * F::DC, koff, ks, dkb, ka);
 #pragma unroll
                 for (int nt = 0; nt < NT; nt++) {
                     float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // two chains
@@ -428,8 +497,8 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             float vsv[2], vbv[2];
 #pragma unroll
             for (int r = 0; r < 2; r++) {
-                vsv[r] = h_load(rec + F::OFF_VS, mtt * 16 + g + 8 * r);
-                vbv[r] = h_load(rec + F::OFF_VB, mtt * 16 + g + 8 * r);
+                vsv[r] = h_load(scl + 4 * D, mtt * 16 + g + 8 * r);
+                vbv[r] = h_load(scl + 4 * D + 2 * P, mtt * 16 + g + 8 * r);
             }
             uint32_t pb[NT][2];                                           // P'^T B fragments of this tile
 #pragma unroll
@@ -452,7 +521,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
                 vbacc[nt][1] = vp.y;
             }
             uint32_t va[MT][4];
-            v_frags<D, BITS>(smem_u32(rec) + F::OFF_VQ + mtt * 16 * F::DC, lane, va);
+            v_frags<D, BITS>(smem_u32(codes) + C::CODES / 2 + mtt * 16 * F::DC, voff, va);
 #pragma unroll
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
@@ -583,6 +652,50 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     }
 }
 
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// the driver's cuTensorMapEncodeTiled (through the runtime's entry-point query: no link against libcuda), or null
+static EncodeTiled encode_tiled() {
+    static EncodeTiled fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return EncodeTiled(nullptr);
+        return reinterpret_cast<EncodeTiled>(p);
+    }();
+    return fn;
+}
+
+// The pool as a 3-D uint8 tensor [sr bytes, block_stride / sr rows, blocks] with sr the widest swizzle row (<= 128,
+// <= a code row) dividing both byte strides; box = one page's K (or V) code rows.  False (plain copies) when no sr
+// >= 32 fits or the driver refuses the map.
+template <int D, int BITS, int P>
+bool make_page_map(const void* cache, int64_t block_stride, int64_t head_stride, CUtensorMap& map, uint32_t& m,
+                   int32_t& rows_per_head, int32_t& box_rows) {
+    constexpr int DC = Fmt<D, BITS, P>::DC;
+    int sr = DC < 128 ? DC : 128;
+    while (sr >= 32 && (block_stride % sr || head_stride % sr)) sr >>= 1;
+    const EncodeTiled enc = encode_tiled();
+    if (sr < 32 || !enc || block_stride / sr > (int64_t(1) << 31) || head_stride / sr > (int64_t(1) << 24)) return false;
+    const cuuint64_t gdim[3] = {cuuint64_t(sr), cuuint64_t(block_stride / sr), cuuint64_t(0x7FFFFFFF)};
+    const cuuint64_t gstride[2] = {cuuint64_t(sr), cuuint64_t(block_stride)};
+    const cuuint32_t box[3] = {cuuint32_t(sr), cuuint32_t(P * DC / sr), 1u};
+    const cuuint32_t estride[3] = {1u, 1u, 1u};
+    const CUtensorMapSwizzle sw = sr == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                  : sr == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(cache), gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    m = uint32_t(sr / 16 - 1);
+    rows_per_head = int32_t(head_stride / sr);
+    box_rows = P * DC / sr;
+    return true;
+}
+
 template <int D, int BITS, int P, int NT, class IN>
 int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
@@ -590,6 +703,13 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
                int32_t n_seqs, cudaStream_t stream) {
     using C = MmaCfg<D, BITS, P, NT>;
     auto kern = decode_mma_kernel<D, BITS, P, NT, IN>;
+    CUtensorMap map;
+    memset(&map, 0, sizeof(map));
+    uint32_t swz_m = 0;
+    int32_t rows_per_head = 0, box_rows = 0;
+    const bool tma = C::SPLIT &&
+                     make_page_map<D, BITS, P>(cache, block_stride, head_stride, map, swz_m, rows_per_head, box_rows);
+    if (!tma) swz_m = 0;
     static unsigned long long attr_set = 0;             // one bit per device: the attribute is per device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -603,7 +723,7 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
                                                    static_cast<const uint8_t*>(cache), block_stride, head_stride,
                                                    static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens,
                                                    max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml,
-                                                   part_o);
+                                                   part_o, map, tma ? 1 : 0, swz_m, rows_per_head, box_rows);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
