@@ -24,6 +24,7 @@ from ._build import PAGE, GpuConfig
 
 _TORCH_DTYPES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32"}
 MAX_SPLITS = 256
+MIN_SPLIT_PAGES = 16
 
 
 def record_bytes(head_dim: int, bits: int, page: int = PAGE) -> int:
@@ -40,14 +41,15 @@ def _byte_strides(cache: torch.Tensor) -> tuple[int, int]:
 
 def split_factor(num_seqs: int, num_kv_heads: int, max_full_pages: int, sms: int, ctas_per_sm: int = 4) -> int:
     """Split-KV factor: enough splits that the decode grid fills the ~ctas_per_sm resident CTAs of every SM once (any
-    integer, not only powers of two), at most MAX_SPLITS and at least 4 pages per split; 1 when the (sequence, kv
-    head) units alone fill half the GPU.  (The reference grows powers of two up to 32 while the grid has fewer than
-    6 blocks per SM, kushkash/_ops.py:182-189; on B200 fewer, fuller splits measured faster: per-split setup, merge
-    and the combine grow with the split count.)"""
+    integer, not only powers of two), at most MAX_SPLITS and at least MIN_SPLIT_PAGES pages per split; 1 when the
+    (sequence, kv head) units alone fill half the GPU.  (The reference grows powers of two up to 32 while the grid
+    has fewer than 6 blocks per SM, kushkash/_ops.py:182-189; on B200 fewer, fuller splits measured faster: per-split
+    setup, merge and the combine grow with the split count -- 8 sequences x 4 kv heads x 64 pages decode fastest at 4
+    splits, not 16.)"""
     units, cap = num_seqs * num_kv_heads, ctas_per_sm * sms
     if units == 0 or units * 2 >= cap or max_full_pages < 8:
         return 1
-    return max(1, min(MAX_SPLITS, cap // units, max_full_pages // 4))
+    return max(1, min(MAX_SPLITS, cap // units, max_full_pages // MIN_SPLIT_PAGES))
 
 
 class Ops:

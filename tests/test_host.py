@@ -72,11 +72,13 @@ def test_split_factor():
     assert split_factor(4, 8, 4096, 148) == 18                    # config 4, one GPU: 32 units x 18 = 576 CTAs
     assert split_factor(4, 1, 4096, 148) == 148                   # config 4, one kv head per GPU
     assert split_factor(1, 1, 7, 148) == 1                        # too few pages to split
-    assert split_factor(1, 1, 16, 148) == 4                       # >= 4 pages per split
+    assert split_factor(1, 1, 16, 148) == 1                       # >= 16 pages per split
+    assert split_factor(1, 1, 64, 148) == 4
+    assert split_factor(8, 4, 64, 148) == 4                       # 4 splits of 16 pages
     assert split_factor(1, 1, 10 ** 6, 148) == 256                # capped
     for S, H, n in ((1, 1, 10 ** 6), (3, 5, 999), (64, 8, 8192)):
         ns = split_factor(S, H, n, 148)
-        assert 1 <= ns <= 256 and (ns == 1 or n // ns >= 4)
+        assert 1 <= ns <= 256 and (ns == 1 or n // ns >= 16)
 
 
 def test_dequant_helpers_roundtrip_on_cpu():
