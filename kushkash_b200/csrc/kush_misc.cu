@@ -5,6 +5,7 @@
 // pair lanes (shuffle xor), strides >= 32 pair a lane's own registers -- then one separately rounded multiply by
 // fp32 1/sqrt(D).  Adds, subtracts and the multiply are correctly rounded IEEE operations in a fixed order, so the
 // result equals the CPU's bit for bit.
+#include "kush_async.cuh"
 #include "kush_common.cuh"
 
 namespace kush {
@@ -120,6 +121,172 @@ __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t* __restrict__
     }
 }
 
+// ------------------------------------------------------------------ vectorised unpack (no rotation)
+// The form both reference callers launch (rot=False: kushkash/vllm/backend.py:848, kushkash/sglang/backend.py:376).
+// One warp per item: a (history page, kv head), a (partial page, kv head) or one new row (all kv heads).  Codes are
+// read 8 bytes at a time (a chunk: 8 channels for int8; 8 + 8 for int4, byte j holding channel j in its low nibble and
+// channel j + D/2 in its high one), dequantized as fma(code, scale, bias) in fp32, rounded once and written with
+// 16-byte stores.  Chunk c of a page is token c / NG, bytes 8 (c % NG) .. + 7 (NG = row bytes / 8, which divides 32);
+// lane l takes chunks l, l + 32, ..., so its channels -- and its K scales -- stay fixed over the page.
+//
+// Codes to fp32 without a conversion instruction: a byte u placed under the exponent of 2^23 (PRMT with 0x4B000000)
+// is the float 2^23 + u, and subtracting 2^23 + OFFS gives u - OFFS exactly.  The stored codes are two's complement;
+// u = code + OFFS is the byte (int8, OFFS 128) or nibble (int4, OFFS 8) with its top bit flipped.
+
+constexpr uint32_t MAGIC_BITS = 0x4B000000u;   // 2^23
+
+template <int OFFS>
+__device__ __forceinline__ void deq8(uint32_t u0, uint32_t u1, const float (&s)[8], const float (&b)[8], float (&o)[8]) {
+    constexpr float M = 8388608.0f + float(OFFS);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        o[k] = __fmaf_rn(__fsub_rn(__uint_as_float(prmt(u0, MAGIC_BITS, 0x7540u + k)), M), s[k], b[k]);
+        o[k + 4] = __fmaf_rn(__fsub_rn(__uint_as_float(prmt(u1, MAGIC_BITS, 0x7540u + k)), M), s[k + 4], b[k + 4]);
+    }
+}
+
+template <class IN>
+__device__ __forceinline__ void store8(IN* dst, const float (&v)[8]) {
+    if constexpr (std::is_same_v<IN, float>) {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            if constexpr (std::is_same_v<IN, __nv_bfloat16>) {
+                const __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+                w[k] = *reinterpret_cast<const uint32_t*>(&p);
+            } else {
+                const __half2 p = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+                w[k] = *reinterpret_cast<const uint32_t*>(&p);
+            }
+        }
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ __forceinline__ void halves8(const uint8_t* p, float (&f)[8]) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+        f[2 * k] = x.x;
+        f[2 * k + 1] = x.y;
+    }
+}
+
+// one chunk of codes (8 bytes) of token row `row` into out (channels 8g.. [+ D/2 + 8g..] of the output row)
+template <int D, int BITS, class IN>
+__device__ __forceinline__ void chunk_out(uint2 w, const float (&s0)[8], const float (&b0)[8], const float (&s1)[8],
+                                          const float (&b1)[8], IN* out) {
+    float o[8];
+    if constexpr (BITS == 4) {
+        deq8<8>((w.x & 0x0F0F0F0Fu) ^ 0x08080808u, (w.y & 0x0F0F0F0Fu) ^ 0x08080808u, s0, b0, o);
+        store8<IN>(out, o);
+        deq8<8>(((w.x >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((w.y >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, s1, b1, o);
+        store8<IN>(out + D / 2, o);
+    } else {
+        deq8<128>(w.x ^ 0x80808080u, w.y ^ 0x80808080u, s0, b0, o);
+        store8<IN>(out, o);
+    }
+}
+
+// tokens [0, n) of the record at rec into rows kout + t * rs, vout + t * rs; K from tk ([P, D], n < P) when given
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void unpack_page_vec(const uint8_t* __restrict__ rec, const IN* __restrict__ tk, int n,
+                                                IN* __restrict__ kout, IN* __restrict__ vout, int64_t rs, int lane) {
+    using F = Fmt<D, BITS, P>;
+    constexpr int NG = F::DC / 8, TPW = WARP / NG, PASSES = P / TPW;
+    static_assert(WARP % NG == 0 && P % TPW == 0, "chunk mapping");
+    const int g = lane % NG, t0 = lane / NG;
+    const int c0 = 8 * g;                                           // first output channel of this lane's chunks
+    if (tk == nullptr) {
+        float s0[8], b0[8], s1[8], b1[8];
+        halves8(rec + F::OFF_KS + 2 * c0, s0);
+        halves8(rec + F::OFF_KB + 2 * c0, b0);
+        if constexpr (BITS == 4) {
+            halves8(rec + F::OFF_KS + 2 * (c0 + D / 2), s1);
+            halves8(rec + F::OFF_KB + 2 * (c0 + D / 2), b1);
+        }
+        uint2 w[PASSES];
+#pragma unroll
+        for (int i = 0; i < PASSES; i++)
+            w[i] = __ldg(reinterpret_cast<const uint2*>(rec + (t0 + TPW * i) * F::DC + c0));
+#pragma unroll
+        for (int i = 0; i < PASSES; i++) chunk_out<D, BITS, IN>(w[i], s0, b0, s1, b1, kout + (t0 + TPW * i) * rs + c0);
+    } else {
+        constexpr int E = 16 / int(sizeof(IN)), CPR = D / E;      // elements per 16 bytes, 16-byte chunks per row
+        for (int c = lane; c < n * CPR; c += WARP) {
+            const int t = c / CPR, q = c % CPR;
+            *reinterpret_cast<uint4*>(kout + t * rs + q * E) = __ldg(reinterpret_cast<const uint4*>(tk + t * D + q * E));
+        }
+    }
+    uint2 w[PASSES];
+    float vs[PASSES], vb[PASSES];
+#pragma unroll
+    for (int i = 0; i < PASSES; i++) {
+        const int t = t0 + TPW * i;
+        if (t < n) {
+            w[i] = __ldg(reinterpret_cast<const uint2*>(rec + F::OFF_VQ + t * F::DC + c0));
+            vs[i] = h_load(rec + F::OFF_VS, t);
+            vb[i] = h_load(rec + F::OFF_VB, t);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < PASSES; i++) {
+        const int t = t0 + TPW * i;
+        if (t < n) {
+            float s[8], b[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) s[k] = vs[i], b[k] = vb[i];
+            chunk_out<D, BITS, IN>(w[i], s, b, s, b, vout + t * rs + c0);
+        }
+    }
+}
+
+// grid (ceil(warps / 8)), block 256; warps = (n_pages + n_tail) * H + n_new.  Records, tail_k, kp and vp 16-byte
+// aligned (the host checks); vec_new: k_new / v_new rows 16-byte aligned, else the new rows are copied by element.
+template <int D, int BITS, int P, class IN>
+__global__ void __launch_bounds__(256) unpack_vec_kernel(
+    const uint8_t* __restrict__ cache, int64_t block_stride, int64_t head_stride, int H,
+    const int32_t* __restrict__ page_blk, const int32_t* __restrict__ page_dst, int n_pages,
+    const int32_t* __restrict__ tail_blk, const int32_t* __restrict__ tail_info, int n_tail,
+    const IN* __restrict__ tail_k, const IN* __restrict__ k_new, const IN* __restrict__ v_new, int64_t ks, int64_t vs,
+    const int32_t* __restrict__ new_dst, int n_new, IN* __restrict__ kp, IN* __restrict__ vp, int vec_new) {
+    const int lane = threadIdx.x % WARP;
+    const int64_t wi = int64_t(blockIdx.x) * (blockDim.x / WARP) + threadIdx.x / WARP;
+    const int64_t rs = int64_t(H) * D;
+    const int64_t n_pw = int64_t(n_pages) * H, n_tw = int64_t(n_tail) * H;
+    if (wi < n_pw + n_tw) {
+        const bool page = wi < n_pw;
+        const int64_t it = page ? wi : wi - n_pw;
+        const int i = int(it / H), h = int(it % H);
+        const uint8_t* rec = cache + int64_t(page ? page_blk[i] : tail_blk[i]) * block_stride + int64_t(h) * head_stride;
+        const int64_t dst0 = page ? page_dst[i] : tail_info[3 * i];
+        const int n = page ? P : tail_info[3 * i + 1];
+        const IN* tk = page ? nullptr : tail_k + (int64_t(tail_info[3 * i + 2]) * H + h) * P * D;
+        unpack_page_vec<D, BITS, P, IN>(rec, tk, n, kp + dst0 * rs + int64_t(h) * D, vp + dst0 * rs + int64_t(h) * D,
+                                        rs, lane);
+    } else if (wi < n_pw + n_tw + n_new) {
+        const int64_t j = wi - n_pw - n_tw;
+        const int64_t o = int64_t(new_dst[j]) * rs;
+        if (vec_new) {
+            constexpr int E = 16 / int(sizeof(IN));
+            for (int64_t c = lane; c < rs / E; c += WARP) {
+                *reinterpret_cast<uint4*>(kp + o + c * E) = __ldg(reinterpret_cast<const uint4*>(k_new + j * ks + c * E));
+                *reinterpret_cast<uint4*>(vp + o + c * E) = __ldg(reinterpret_cast<const uint4*>(v_new + j * vs + c * E));
+            }
+        } else {
+            for (int64_t c = lane; c < rs; c += WARP) {
+                kp[o + c] = k_new[j * ks + c];
+                vp[o + c] = v_new[j * vs + c];
+            }
+        }
+    }
+}
+
 }  // namespace kush
 
 using namespace kush;
@@ -157,6 +324,22 @@ extern "C" int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, i
     if (!cache || !kp || !vp) return set_error(KUSH_ERR_ARG, "kush_sm100_unpack: null pointer");
     int rc = dispatch_fmt(head_dim, bits, page, dtype, [&](auto D, auto B, auto P, auto in) {
         using IN = decltype(in);
+        const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+        const bool vec = !rot && a16(cache) && block_stride % 16 == 0 && head_stride % 16 == 0 && a16(kp) && a16(vp) &&
+                         (n_tail == 0 || a16(tail_k));
+        if (vec) {
+            const int64_t es = int64_t(sizeof(IN));
+            const int vec_new = n_new > 0 && a16(k_new) && a16(v_new) && (k_stride * es) % 16 == 0 &&
+                                (v_stride * es) % 16 == 0;
+            const int64_t warps = (int64_t(n_pages) + n_tail) * hkv + n_new;
+            unpack_vec_kernel<D.value, B.value, P.value, IN>
+                <<<unsigned((warps + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+                    static_cast<const uint8_t*>(cache), block_stride, head_stride, hkv, page_blk, page_dst, n_pages,
+                    tail_blk, tail_info, n_tail, static_cast<const IN*>(tail_k), static_cast<const IN*>(k_new),
+                    static_cast<const IN*>(v_new), k_stride, v_stride, new_dst, n_new, static_cast<IN*>(kp),
+                    static_cast<IN*>(vp), vec_new);
+            return check_launch("kush_sm100_unpack");
+        }
         dim3 grid(unsigned(blocks), hkv);
         unpack_kernel<D.value, B.value, P.value, IN><<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
             static_cast<const uint8_t*>(cache), block_stride, head_stride, hkv, page_blk, page_dst, n_pages, tail_blk,

@@ -147,23 +147,49 @@ def test_fwht_bit_exact(D, dtype):
     assert torch.equal(gpu_ops(D, 4, 1, dtype).fwht(xc, out=xc).cpu(), got)        # in place
 
 
-@pytest.mark.parametrize("rot", [False, True])
-@pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("D,bits", [(64, 4), (128, 4), (256, 4), (128, 8), (64, 8)])
-def test_unpack_bit_exact(D, bits, dtype, rot):
-    c = unpack_inputs(D, bits)
+def unpack_case(D, bits, P, dtype, rot, new_pad=0):
+    """Oracle and GPU unpack of one seeded case; new_pad > 0 gives k_new / v_new rows a stride of H * D + new_pad
+    elements (views into wider buffers), which takes the element-wise copy of the new rows."""
+    c = unpack_inputs(D, bits, P)
     names = ("page_blk", "page_dst", "tail_blk", "tail_info", "tail_k", "k_new", "v_new", "new_dst")
     shape = (c["rows"], c["H"], D)
     args = {n: c[n] for n in names}
     for n in ("tail_k", "k_new", "v_new"):
         args[n] = exact(args[n], dtype)
     rk, rv = torch.full(shape, float("nan")), torch.full(shape, float("nan"))
-    OracleOps(D, bits, 1).unpack(c["records"], *[args[n] for n in names], rk, rv, rot)
+    OracleOps(D, bits, 1, P).unpack(c["records"], *[args[n] for n in names], rk, rv, rot)
     # NaN-filled on the host so untouched rows carry the same NaN bit pattern as the reference's
     kp = torch.full(shape, float("nan")).to(dtype).cuda()
     vp = torch.full(shape, float("nan")).to(dtype).cuda()
     gargs = [args[n].cuda().to(dtype) if n in ("tail_k", "k_new", "v_new") else args[n].cuda() for n in names]
-    gpu_ops(D, bits, 1, dtype).unpack(c["records"].cuda(), *gargs, kp, vp, rot)
+    if new_pad:
+        for i in (5, 6):
+            x = gargs[i]
+            wide = torch.zeros(x.shape[0], x.shape[1] * D + new_pad, dtype=dtype, device="cuda")
+            wide[:, :x.shape[1] * D] = x.reshape(x.shape[0], -1)
+            gargs[i] = wide[:, :x.shape[1] * D].view(x.shape[0], x.shape[1], D)
+            assert gargs[i].stride(0) == x.shape[1] * D + new_pad
+    gpu_ops(D, bits, 1, dtype, P).unpack(c["records"].cuda(), *gargs, kp, vp, rot)
+    return kp, vp, rk, rv
+
+
+@pytest.mark.parametrize("rot", [False, True])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("P", [16, 32])
+@pytest.mark.parametrize("D,bits", [(64, 4), (128, 4), (256, 4), (128, 8), (64, 8), (256, 8)])
+def test_unpack_bit_exact(D, bits, P, dtype, rot):
+    kp, vp, rk, rv = unpack_case(D, bits, P, dtype, rot)
+    for got, want in ((kp.cpu(), rk.to(dtype)), (vp.cpu(), rv.to(dtype))):
+        a = got.view(torch.int16) if dtype != torch.float32 else got.view(torch.int32)
+        b = want.view(torch.int16) if dtype != torch.float32 else want.view(torch.int32)
+        assert torch.equal(a, b), f"{(a != b).sum().item()} of {a.numel()} values differ"
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("pad", [1, 3, 8])
+def test_unpack_strided_new_rows(pad, dtype):
+    """New rows whose row stride is not a multiple of 16 bytes (pad 1, 3) and one that is (pad 8)."""
+    kp, vp, rk, rv = unpack_case(128, 4, 16, dtype, False, new_pad=pad)
     for got, want in ((kp.cpu(), rk.to(dtype)), (vp.cpu(), rv.to(dtype))):
         a = got.view(torch.int16) if dtype != torch.float32 else got.view(torch.int32)
         b = want.view(torch.int16) if dtype != torch.float32 else want.view(torch.int32)
