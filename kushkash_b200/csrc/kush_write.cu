@@ -499,7 +499,8 @@ struct WS {
     static constexpr int NPR = BITS == 4 ? 2 * NU : NU;             // channel pairs per lane
     static constexpr bool KREG = TPS * KWD <= 32;                   // keep the K words in registers between passes
     __host__ __device__ static constexpr int kpos(int t) { return t * RSTR + (t / TPS) * KGAP; }
-    static_assert(P == 16 * G && NW % G == 0 && P % RPP == 0 && NW * NS * 8 <= OFF_STAGE && VOFF % 16 == 0,
+    static_assert(P == 16 * G && NW % G == 0 && P % RPP == 0 && NW * NS * 8 <= OFF_STAGE && VOFF % 16 == 0 &&
+                      STAGE >= P * ROWB && STAGE % 16 == 0,
                   "geometry");
 };
 
@@ -836,6 +837,45 @@ struct WMeta {
     int row0, hf, blk, s, pg, q0, ctx, total;
 };
 
+// one warp: n rows of D 16-bit values (row r at src + r * ss, 16-byte aligned) into shared memory dst (rows packed)
+// by 16-byte cp.async copies, all in flight together; cp_async_wait_warp waits for them and publishes them to the warp
+template <int D, class IN>
+__device__ __forceinline__ void stage_rows_warp(IN* dst, const IN* src, int64_t ss, int n, int lane) {
+    constexpr int CPR = D * int(sizeof(IN)) / 16, E = 16 / int(sizeof(IN));
+    const uint32_t d0 = smem_u32(dst);
+    for (int c = lane; c < n * CPR; c += WARP) {
+        const int r = c / CPR, q = c % CPR;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + uint32_t((r * D + q * E) * int(sizeof(IN)))),
+                     "l"(src + r * ss + q * E)
+                     : "memory");
+    }
+}
+
+__device__ __forceinline__ void cp_async_wait_warp() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+}
+
+// one warp: n rows of D 16-bit values from src (row stride ss) to dst (rows packed) in global memory, 16-byte
+// accesses, four loads per lane in flight before their stores (src is not written by the kernel)
+template <int D, class IN>
+__device__ __forceinline__ void copy_rows_warp(IN* dst, const IN* __restrict__ src, int64_t ss, int n, int lane) {
+    constexpr int CPR = D * int(sizeof(IN)) / 16, E = 16 / int(sizeof(IN)), B = 4;
+    for (int c0 = lane; c0 < n * CPR; c0 += B * WARP) {
+        uint4 v[B];
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            const int c = c0 + b * WARP;
+            if (c < n * CPR) v[b] = __ldg(reinterpret_cast<const uint4*>(src + (c / CPR) * ss + (c % CPR) * E));
+        }
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            const int c = c0 + b * WARP;
+            if (c < n * CPR) *reinterpret_cast<uint4*>(dst + (c / CPR) * D + (c % CPR) * E) = v[b];
+        }
+    }
+}
+
 template <int D, int BITS, int P, class IN>
 __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
     write_stream_kernel(const IN* __restrict__ k_new, const IN* __restrict__ v_new, int64_t k_stride, int64_t v_stride,
@@ -904,18 +944,19 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
                          : "memory");
         }
     };
-    // every other item: the warp-level per-token path (mode 0 / 1 / 2 as write_kernel) by the role-0 warp of the
-    // stream, its slot i % NS as scratch
+    // every other item: the per-token path (mode 0 / 1 / 2 as write_kernel) by the role-0 warp of the stream, its
+    // slot i % NS as the page's staging rows: [split old tail rows][new rows], loaded by cp.async all at once
     auto general = [&](int i, int l, int h, int blk) {
         const int64_t ps = int64_t(KUSH_META(pg, false, l)) * P, ctx = KUSH_META(ctx, false, l);
         const int64_t total = KUSH_META(total, false, l), q0 = KUSH_META(q0, false, l);
         const int s = KUSH_META(s, false, l);
-        const int64_t tb = (int64_t(tail_idx[s]) * H + h) * P * D;
+        const int64_t tb = (int64_t(tail_idx[s]) * H + h) * P * D, hd = int64_t(h) * D;
         const bool complete = ps + P <= total;
         auto stash = [&](int64_t pstart) {
-            for (int64_t t = max(pstart, ctx); t < total; t++)
-                for (int d = lane; d < D; d += WARP)
-                    tail_k[tb + (t - pstart) * D + d] = k_new[(q0 + t - ctx) * k_stride + int64_t(h) * D + d];
+            const int64_t t0 = max(pstart, ctx);
+            if (t0 < total)
+                copy_rows_warp<D, IN>(tail_k + tb + (t0 - pstart) * D, k_new + (q0 + t0 - ctx) * k_stride + hd, k_stride,
+                                      int(total - t0), lane);
         };
         if (mode == 1) {
             if (!complete) stash(ps);
@@ -924,20 +965,25 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
         uint8_t* rec = rec_at(cache, blk, h, block_stride, head_stride);
         const int r0 = int(max(ps, ctx) - ps), r1 = int(min(ps + P, total) - ps);
         const int split = complete ? int(max(int64_t(0), min(int64_t(P), ctx - ps))) : 0;
-        IN* kold = reinterpret_cast<IN*>(slots + (i % C::NS) * C::STAGE);        // [split][D] old tail rows
-        for (int e = lane; e < split * D; e += WARP) kold[e] = tail_k[tb + e];
-        __syncwarp();
+        IN* stage = reinterpret_cast<IN*>(slots + (i % C::NS) * C::STAGE);
+        stage_rows_warp<D, IN>(stage, tail_k + tb, D, split, lane);                  // old tail rows, before a stash
+        stage_rows_warp<D, IN>(stage + split * D, v_new + (q0 + ps + r0 - ctx) * v_stride + hd, v_stride, r1 - r0,
+                               lane);
+        cp_async_wait_warp();
         if (mode == 2) {
             const int64_t f0 = (ctx / P) * P, last = ((total - 1) / P) * P;
             const bool last_partial = total % P != 0 && total > ctx;
             const bool first_reads_tail = ctx % P != 0 && f0 + P <= total;
             if (last_partial && ((first_reads_tail && last != f0) ? ps == f0 : ps == last)) stash(last);
         }
-        for (int r = r0; r < r1; r++)
-            quantize_v_row<D, BITS, P, IN>(v_new + (q0 + ps + r - ctx) * v_stride + int64_t(h) * D, rec, r, lane);
-        if (complete)
-            quantize_k_page<D, BITS, P, IN>(kold, D, k_new + (q0 + ps + split - ctx) * k_stride + int64_t(h) * D,
-                                            k_stride, split, rec, lane, WARP);
+        for (int r = r0; r < r1; r++) quantize_v_row<D, BITS, P, IN>(stage + (split + r - r0) * D, rec, r, lane);
+        if (complete) {
+            __syncwarp();                                                            // V rows read: reuse for K
+            stage_rows_warp<D, IN>(stage + split * D, k_new + (q0 + ps + split - ctx) * k_stride + hd, k_stride,
+                                   P - split, lane);
+            cp_async_wait_warp();
+            quantize_k_page<D, BITS, P, IN>(stage, D, stage + split * D, D, split, rec, lane, WARP);
+        }
         __syncwarp();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the slot may next be filled by a bulk copy
     };
