@@ -19,6 +19,7 @@ algorithmic bytes / its CUDA-event duration vs the measured HBM copy peak); the 
     python bench.py --workload long           # BASELINE config 4 (kv heads partitioned over the GPUs)
     python bench.py --workload mix            # BASELINE config 5 (serving mix: prompt writes + ragged decode)
     python bench.py --workload c1 | c2        # BASELINE configs 1 and 2 (single-layer Qwen2.5-7B geometry)
+    python bench.py --workload unpack         # prefill with history: records -> packed bf16 K/V (unpack)
     python bench.py --impl reference          # the reference's CPU algorithm (C restatement) on the host cores
     torchrun --nproc-per-node N bench.py --gpus N ...
 """
@@ -332,9 +333,10 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["batch", "long", "mix", "c1", "c2"], default="batch",
+    ap.add_argument("--workload", choices=["batch", "long", "mix", "c1", "c2", "unpack"], default="batch",
                     help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned); "
-                         "mix: config 5 (serving mix); c1, c2: configs 1 and 2 (single layer; requests partitioned)")
+                         "mix: config 5 (serving mix); c1, c2: configs 1 and 2 (single layer; requests partitioned); "
+                         "unpack: prefill with history (packed K/V for a prefill attention)")
     a = ap.parse_args()
     if a.workload == "long":
         for k, v in (("batch", 4), ("context", 131072), ("page", 32), ("layers", 8)):
@@ -342,6 +344,8 @@ def main() -> None:
                 setattr(a, k, v)
     if a.workload == "mix" and a.layers == ap.get_default("layers"):
         a.layers = 4
+    if a.workload == "unpack" and a.layers == ap.get_default("layers"):
+        a.layers = 8
     if a.warmup < 3 and a.impl == "ours":
         print("bench.py: --warmup < 3 is raised to 3 (timing rule)", file=sys.stderr)
         a.warmup = 3
@@ -351,7 +355,13 @@ def main() -> None:
     geo = Geometry(a)
 
     if a.impl == "reference":
-        run_reference(a, geo, world, rank)
+        if a.workload == "unpack":
+            run_reference_unpack(a, world, rank)
+        else:
+            run_reference(a, geo, world, rank)
+        return
+    if a.workload == "unpack":
+        run_unpack(a, world, rank, local)
         return
     if a.workload == "long":
         run_long(a, world, rank, local)
@@ -982,6 +992,274 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- unpack: prefill with history
+UNPACK_METRIC = "unpack (prefill with history): algorithmic HBM GB/s"
+
+
+class UnpackGeo:
+    """The packed-prefill group of the vLLM / SGLang backends' prefill with history, per GPU and layer: S sequences
+    of `hist` cached tokens -- full 16-token pages and a partial last page whose exact K sits in the tail slot -- and a
+    new chunk of C rows each, unpacked by one launch into one [rows, 8, 128] workspace (the backends' ws.k / ws.v)."""
+
+    def __init__(self, S: int = 32, hist: int = 4103, C: int = 512, L: int = 8):
+        self.S, self.hist, self.C, self.L = S, hist, C, L
+        self.D, self.H, self.P, self.bits = 128, 8, 16, 4
+        self.DC = self.D // 2
+        self.RB = 2 * self.P * self.DC + 4 * self.D + 4 * self.P
+        self.fp, self.part = hist // self.P, hist % self.P
+        self.npg = -(-hist // self.P)
+        self.rows_per = hist + C
+
+    def launch_bytes(self, S: int | None = None) -> int:
+        """Algorithmic bytes of one layer's unpack over S sequences: full pages (record in, bf16 K and V rows out),
+        the partial page (V code rows and scales, exact K rows in; K and V rows out), the new chunk (bf16 K and V in
+        and out) and the int32 indices."""
+        S = self.S if S is None else S
+        H, D, P, part, C = self.H, self.D, self.P, self.part, self.C
+        pages = self.fp * H * (self.RB + 2 * P * D * 2)
+        partial = H * part * (self.DC + 4 + D * 2 + 2 * D * 2)
+        new = C * H * D * 2 * 4
+        return S * (pages + partial + new + 4 * (2 * self.fp + 4 + C))
+
+    def indices(self, S: int) -> dict:
+        """Host int32 unpack indices for S sequences with block table rows s * npg .. (identity table)."""
+        fp, P = self.fp, self.P
+        base = torch.arange(S, dtype=torch.int32) * self.rows_per
+        bt = torch.arange(S * self.npg, dtype=torch.int32).view(S, self.npg)
+        return {"page_blk": bt[:, :fp].reshape(-1).contiguous(),
+                "page_dst": (base[:, None] + torch.arange(fp, dtype=torch.int32)[None] * P).reshape(-1).contiguous(),
+                "tail_blk": bt[:, fp].contiguous(),
+                "tail_info": torch.stack([base + fp * P, torch.full((S,), self.part, dtype=torch.int32),
+                                          torch.arange(S, dtype=torch.int32)], 1).reshape(-1).contiguous(),
+                "new_dst": (base[:, None] + self.hist + torch.arange(self.C, dtype=torch.int32)[None]).reshape(-1)
+                .contiguous()}
+
+    def describe(self) -> dict:
+        return {"workload": f"prefill with history (unpack): Llama-3.1-8B kv geometry (8 kv heads, head_dim 128), "
+                            f"int4, page 16; {self.S} sequences x {self.hist} cached tokens ({self.fp} full pages + a "
+                            f"{self.part}-token partial page) + a {self.C}-row new chunk each, {self.L} layers per step",
+                "model": "Llama-3.1-8B (attention geometry only)", "global_batch": self.S, "seq_len": self.rows_per,
+                "layers": self.L,
+                "l2": "inputs larger than L2 (%.2f GB of records and new rows per step)" % (
+                    self.L * self.S * (self.npg * self.H * self.RB + 2 * self.C * self.H * self.D * 2) / 1e9)}
+
+
+def unpack_jobs(geo: UnpackGeo, S: int):
+    """Bulk-write arguments for S whole histories: query_start_loc, job (seq, page)."""
+    qsl = torch.arange(S + 1, dtype=torch.int32) * geo.hist
+    js = torch.arange(S, dtype=torch.int32).repeat_interleave(geo.npg)
+    jp = torch.arange(geo.npg, dtype=torch.int32).repeat(S)
+    return qsl, js, jp
+
+
+class UnpackEngine:
+    """One GPU's unpack workload: L layers of caches filled by the bulk quantize-on-write from seeded K / V, a seeded
+    random block table, every layer's new rows, one shared output workspace."""
+
+    def __init__(self, geo: UnpackGeo, device: torch.device, seed: int):
+        from kushkash_b200 import Ops
+        g = self.geo = geo
+        S, H, D, P, L = g.S, g.H, g.D, g.P, g.L
+        self.ops = Ops(device, D, g.bits, 4, torch.bfloat16, P)
+        gen = torch.Generator().manual_seed(seed)
+        dgen = torch.Generator(device=device).manual_seed(seed + 1)
+        perm = torch.randperm(S * g.npg, generator=gen).to(torch.int32)
+        bt = perm.view(S, g.npg)
+        self.pool = torch.zeros(L, S * g.npg, H, g.RB, dtype=torch.uint8, device=device)
+        self.tail = torch.zeros(L, S, H, P, D, dtype=torch.bfloat16, device=device)
+        ti = torch.arange(S, dtype=torch.int32, device=device)
+        offsets = offsets_llama(H, D, gen).to(device)
+        qsl, js, jp = (x.to(device) for x in unpack_jobs(g, S))
+        for layer in range(L):
+            k = (torch.randn(S * g.hist, H, D, generator=dgen, device=device) + offsets).to(torch.bfloat16)
+            v = torch.randn(S * g.hist, H, D, generator=dgen, device=device).to(torch.bfloat16)
+            sl = torch.full((S,), g.hist, dtype=torch.int32, device=device)
+            self.ops.write(k, v, qsl, sl, ti, js, jp, self.pool[layer], bt.to(device), self.tail[layer])
+            del k, v
+        idx = g.indices(S)
+        idx["page_blk"] = bt[:, :g.fp].reshape(-1).contiguous()          # the random table's blocks
+        idx["tail_blk"] = bt[:, g.fp].contiguous()
+        self.idx = {k: v.to(device) for k, v in idx.items()}
+        self.k_new = (torch.randn(L, S * g.C, H, D, generator=dgen, device=device) + offsets).to(torch.bfloat16)
+        self.v_new = torch.randn(L, S * g.C, H, D, generator=dgen, device=device).to(torch.bfloat16)
+        self.kp = torch.empty(S * g.rows_per, H, D, dtype=torch.bfloat16, device=device)
+        self.vp = torch.empty_like(self.kp)
+        torch.cuda.synchronize(device)
+
+    def unpack(self, layer: int) -> None:
+        x = self.idx
+        self.ops.unpack(self.pool[layer], x["page_blk"], x["page_dst"], x["tail_blk"], x["tail_info"],
+                        self.tail[layer], self.k_new[layer], self.v_new[layer], x["new_dst"], self.kp, self.vp,
+                        rot=False)
+
+    def step(self) -> None:
+        for layer in range(self.geo.L):
+            self.unpack(layer)
+
+
+def time_cpu_unpack(geo: UnpackGeo, seqs: int, budget_s: float, min_calls: int = 1) -> dict:
+    """The reference's CPU unpack (kushkash/kush/cpu.mojo:110-169, one thread; its C restatement in oracle/) over
+    `seqs` sequences of one layer written by the oracle's bulk write, until budget_s; value in the same algorithmic
+    bytes as the GPU figure."""
+    from oracle.kush_oracle import OracleOps
+    g = geo
+    H, D, P = g.H, g.D, g.P
+    gen = torch.Generator().manual_seed(99)
+    ops = OracleOps(D, g.bits, 1, P)
+    pool = torch.zeros(seqs * g.npg, H, g.RB, dtype=torch.uint8)
+    tail = torch.zeros(seqs, H, P, D)
+    off = offsets_llama(H, D, gen)
+    qsl, js, jp = unpack_jobs(g, seqs)
+    k = (torch.randn(seqs * g.hist, H, D, generator=gen) + off).bfloat16().float()
+    v = torch.randn(seqs * g.hist, H, D, generator=gen).bfloat16().float()
+    bt = torch.arange(seqs * g.npg, dtype=torch.int32).view(seqs, g.npg)
+    ops.write(k, v, qsl, torch.full((seqs,), g.hist, dtype=torch.int32), torch.arange(seqs, dtype=torch.int32),
+              js, jp, pool, bt, tail)
+    x = g.indices(seqs)
+    kn = (torch.randn(seqs * g.C, H, D, generator=gen) + off).bfloat16().float()
+    vn = torch.randn(seqs * g.C, H, D, generator=gen).bfloat16().float()
+    kp = torch.empty(seqs * g.rows_per, H, D)
+    vp = torch.empty_like(kp)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        ops.unpack(pool, x["page_blk"], x["page_dst"], x["tail_blk"], x["tail_info"], tail, kn, vn, x["new_dst"],
+                   kp, vp, False)
+        calls += 1
+        el = time.perf_counter() - t0
+        if calls >= min_calls and el >= budget_s:
+            break
+    return {"value": round(calls * g.launch_bytes(seqs) / el / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{calls} unpacks of {seqs} of the {g.S} sequences (one layer), {el:.1f} s; fp32 output, bytes "
+                      "counted as for the bf16 workload", "calls": calls, "seconds": el}
+
+
+def unpack_traffic() -> float | None:
+    """DRAM bytes per unpack launch at this workload from the committed ncu summary (profiles/), if present."""
+    p = ROOT / "profiles" / "unpack_traffic.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["total"])
+    return None
+
+
+def run_unpack(a, world: int, rank: int, local: int) -> None:
+    """Prefill with history: K steps of L unpack launches (one CUDA graph per step); requests partitioned over the
+    GPUs, no collective (weak scaling)."""
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    geo = UnpackGeo(L=a.layers)
+    eng = UnpackEngine(geo, dev, seed=77 + rank)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(a.warmup - 1):
+        eng.step()
+    graph = capture(eng.step, dev)
+    graph.replay()
+    barrier()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    # ---- e2e: the step's inputs (indices and every layer's new rows) from pinned host memory; back, the last packed
+    # row of each sequence (K and V) -- the packed buffers themselves feed an attention kernel on the device
+    hidx = {k: v.cpu().pin_memory() for k, v in eng.idx.items()}
+    hk, hv = eng.k_new.cpu().pin_memory(), eng.v_new.cpu().pin_memory()
+    last = torch.arange(1, geo.S + 1, device=dev) * geo.rows_per - 1
+    hout = torch.empty(2, geo.S, geo.H, geo.D, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        for k_, t in hidx.items():
+            eng.idx[k_].copy_(t, non_blocking=True)
+        eng.k_new.copy_(hk, non_blocking=True)
+        eng.v_new.copy_(hv, non_blocking=True)
+        graph.replay()
+        hout[0].copy_(eng.kp[last], non_blocking=True)
+        hout[1].copy_(eng.vp[last], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    x1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = x0.elapsed_time(x1)
+    h2d = sum(t.numel() * t.element_size() for t in hidx.values()) + 2 * hk.numel() * hk.element_size()
+    d2h = hout.numel() * hout.element_size()
+    if dist is not None:
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = (float(v) for v in t.tolist())
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = time_cpu_unpack(geo, 2, a.cpu_seconds)
+        for k_ in ("calls", "seconds"):
+            cpu.pop(k_)
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        step_bytes = geo.launch_bytes() * geo.L * world
+        per_launch_ms = ms / (a.steps * geo.L)
+        achieved = geo.launch_bytes() / (per_launch_ms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": UNPACK_METRIC, "value": round(step_bytes * a.steps / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 records, bf16 new rows and output, fp32 dequant",
+            "data": "synthetic (seeded bf16 N(0,1) K/V with per-channel key offsets, written by the bulk write)",
+            "config": {**geo.describe(), "parallelism": f"requests partitioned over {world} GPU(s), no collective"},
+            "e2e": {"value": round(step_bytes * a.steps / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms / a.steps, 4)},
+            "roofline": {"kernel": "kush_sm100_unpack", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": f"{peak_kind} (HBM copy, MEASURED_PEAKS.json)" if peak_kind == "measured"
+                         else "fallback", "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": unpack_traffic(), "algorithmic_bytes_per_launch": geo.launch_bytes(),
+                         "us_per_launch": round(per_launch_ms * 1e3, 2)},
+            "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": a.steps * geo.L}), flush=True)
+    del graph, eng
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_unpack(a, world: int, rank: int) -> None:
+    """The reference arm of the unpack workload: the reference's CPU unpack (one thread; its C restatement) on the
+    host, each step one unpack of 2 of the sequences.  Rank 0 only."""
+    if rank != 0:
+        return
+    from oracle.kush_oracle import build
+    build()
+    geo = UnpackGeo(L=a.layers)
+    r = time_cpu_unpack(geo, 2, 0.0, min_calls=a.warmup)
+    r = time_cpu_unpack(geo, 2, 0.0, min_calls=a.steps)
+    value = r["value"]
+    res = {"value": value, "unit": "GB/s", "cores": 1, "kind": "port",
+           "sample": f"{a.steps} unpacks of 2 of the {geo.S} sequences (one layer), fp32 output"}
+    print(json.dumps({"metric": UNPACK_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+                      "warmup": a.warmup, "ms_per_step": round(r["seconds"] / r["calls"] * 1e3, 3),
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "int4 records, fp32 compute", "impl": "reference", "data": "synthetic (seeded)",
+                      "config": {**geo.describe(), "parallelism": "one host thread"}, "cpu_baseline": res,
+                      "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
 
 
 def run_reference(a, geo: Geometry, world: int, rank: int) -> None:
