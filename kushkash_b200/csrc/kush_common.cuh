@@ -109,6 +109,34 @@ __device__ __forceinline__ float warp_sum(float x) {
     return x;
 }
 
+// ------------------------------------------------------------------ split-KV page ranges
+// The reference gives split z of a sequence with `full` full pages the range [z q, (z+1) q), q = ceil(full /
+// n_splits) (kushkash/kush/gpu.mojo:418-424): every sequence in n_splits pieces, however short.  Here the quota is
+// one for the batch, q = ceil(max_full / n_splits) over the batch's sequences: a short sequence fills only its first
+// ceil(full / q) splits and its other splits have nothing to do (they only mark their partials empty), so the
+// splits go to the long sequences of a ragged batch and no CTA is left with a page or two.  With equal lengths the
+// ranges are the reference's.  The tail page belongs to the last split with pages (split 0 when there are none).
+// Every warp of a CTA computes the same range (the max is a warp reduction over seq_lens).
+struct SplitRange {
+    int64_t p0, p1;      // full pages [p0, p1)
+    bool active;         // this split has pages, or is split 0
+    bool last;           // this split takes the tail page
+};
+
+__device__ __forceinline__ SplitRange split_range(const int32_t* seq_lens, int n_seqs, int s, int z, int n_splits,
+                                                  int P) {
+    const uint32_t full = uint32_t(seq_lens[s]) / uint32_t(P);
+    if (n_splits == 1) return {0, int64_t(full), true, true};
+    uint32_t mx = 0;
+    for (int i = threadIdx.x % WARP; i < n_seqs; i += WARP) mx = max(mx, uint32_t(seq_lens[i]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const uint32_t q = max(1u, (mx / uint32_t(P) + uint32_t(n_splits) - 1) / uint32_t(n_splits));   // pages per split
+    const uint32_t p0 = min(full, uint32_t(z) * q), p1 = min(full, p0 + q);
+    const bool active = z == 0 || p0 < full;
+    return {int64_t(p0), int64_t(p1), active, active && p1 == full};
+}
+
 // ------------------------------------------------------------------ host-side dispatch
 template <int V> using IC = std::integral_constant<int, V>;
 

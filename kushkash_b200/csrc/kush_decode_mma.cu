@@ -4,7 +4,8 @@
 // where the K scale and bias enter (below), the rest -- page-granular online softmax, V scale folded into the
 // softmax weights and V bias into one scalar per head, exact-K tail, warp merge, split-KV partials -- is the same.
 //
-// Work split: grid (S, Hkv, n_splits), 4 warps per CTA.  Split z owns a contiguous page range; warp w takes pages
+// Work split: grid (S, Hkv, n_splits), 4 warps per CTA.  Split z owns a contiguous page range (split_range: one
+// page quota per split for the batch, splits past a sequence's end return at once); warp w takes pages
 // start + w, start + w + 4, ...  Each warp streams its pages through its own ring of NS shared-memory slots with
 // one 1-D bulk copy per page record (cp.async.bulk, completion on an mbarrier; no multicast), issued NS pages
 // ahead by lane 0, with the block-table entries prefetched 32 pages at a time into registers.  All waits are
@@ -297,9 +298,10 @@ struct MmaCfg {
     static constexpr int RING = MMA_NW * NS * RB > MERGE ? MMA_NW * NS * RB : (MERGE + 127) / 128 * 128;
     static constexpr int BARS = (8 * MMA_NW * NS + 127) / 128 * 128;
     // shared memory: [bars | pad to 1024 | ring: int8 code slots [NW][NS][CODES] + scale slots [NW][NS][SCALES], int4
-    // record slots [NW][NS][RB] (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D])]; the pad aligns
+    // record slots [NW][NS][RB] (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D]) | kb_ref (fp16,
+    // [D])]; the pad aligns
     // the code slots to the swizzle period
-    static constexpr int SMEM = 1024 + BARS + RING + 4 * (GMAX * D + D);
+    static constexpr int SMEM = 1024 + BARS + RING + 4 * (GMAX * D + D) + 2 * D;
     static_assert(!SPLIT || (CODES % 1024 == 0 && SCALES % 16 == 0), "code slots must keep the swizzle period");
     // CTAs per SM the register budget targets (the larger tiles need more registers per thread)
     static constexpr int MINB = (D == 64 || (D == 128 && NT == 1 && !(BITS == 8 && P == 32))) ? 4
@@ -328,13 +330,22 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     uint8_t* ring = smem + (((smem0 + C::BARS + 1023u) & ~1023u) - smem0);   // code + scale slots, reused by the merge
     float* qsm = reinterpret_cast<float*>(ring + C::RING);              // [G][D] q * scale * log2e
     float* kbr = qsm + G * D;                                           // [D] kb_ref
+    __half* kb16 = reinterpret_cast<__half*>(kbr + D);                  // [D] kb_ref as fp16 (read in K pair order)
     const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
     const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP, g = lane >> 2, tid = lane & 3;
     const int64_t n = seq_lens[s];
     const int tail_n = int(n % P);
     const int64_t full = n / P;
-    const int64_t pps = (full + n_splits - 1) / n_splits;
-    const int64_t p0 = min(full, int64_t(z) * pps), p1 = min(full, p0 + pps);
+    const SplitRange sr = split_range(seq_lens, int(gridDim.x), s, z, n_splits, P);
+    if (!sr.active) {                                                   // no pages here: an empty partial
+        for (int hd = threadIdx.x; hd < G; hd += NW * WARP) {
+            const int64_t pb = ((int64_t(s) * H + h) * n_splits + z) * G + hd;
+            part_ml[pb * 2] = -INFINITY;
+            part_ml[pb * 2 + 1] = 0.0f;
+        }
+        return;
+    }
+    const int64_t p0 = sr.p0, p1 = sr.p1;
     const int32_t* bt = block_table + int64_t(s) * max_pages;
     const int64_t qbase = (int64_t(s) * H + h) * G * D;
     const uint8_t* hcache = cache + int64_t(h) * head_stride;
@@ -383,12 +394,18 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm_log2;
     // kb_ref: K bias of the sequence's first page (only when one is full; a tail-only sequence uses 0)
     const uint8_t* rec0 = full > 0 ? hcache + int64_t(bt[0]) * block_stride : nullptr;
-    for (int i = threadIdx.x; i < D; i += NW * WARP) kbr[i] = rec0 ? h_load(rec0 + F::OFF_KB, i) : 0.0f;
+    for (int i = threadIdx.x; i < D; i += NW * WARP) {
+        const __half kb = rec0 ? reinterpret_cast<const __half*>(rec0 + F::OFF_KB)[i] : __float2half_rn(0.0f);
+        kbr[i] = __half2float(kb);
+        kb16[i] = kb;
+    }
     __syncthreads();
 
-    // B fragments: Qh^T for heads nt*8 + g at this lane's K pairs; kb_ref pairs
+    // B fragments: Qh^T for heads nt*8 + g at this lane's K pairs; the kb_ref pairs in registers for 16-token pages,
+    // read per tile from kb16 for 32-token pages (whose two tiles per page need the 16 registers)
+    constexpr bool KREF_REGS = P == 16;
     uint32_t bq[NT][2 * KT];
-    uint32_t kref[2 * KT];
+    uint32_t kref_r[KREF_REGS ? 2 * KT : 1];
 #pragma unroll
     for (int e = 0; e < 2 * KT; e++) {
         const int d = L::kdim(tid, e);
@@ -397,7 +414,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             const int head = nt * 8 + g;
             bq[nt][e] = head < G ? pack_h2(qsm[head * D + d], qsm[head * D + d + 1]) : 0u;
         }
-        kref[e] = pack_h2(kbr[d], kbr[d + 1]);
+        if constexpr (KREF_REGS) kref_r[e] = pack_h2(kbr[d], kbr[d + 1]);
     }
 
     float o[MT][NT][4];                                                  // O^T accumulators
@@ -440,8 +457,15 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
                 uint32_t ks[2 * KT], dkb[2 * KT];
                 load_pairs<D, BITS>(scl, tid, ks);
                 load_pairs<D, BITS>(scl + 2 * D, tid, dkb);
+                if constexpr (KREF_REGS) {
 #pragma unroll
-                for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref[e]);
+                    for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref_r[e]);
+                } else {
+                    uint32_t kref[2 * KT];
+                    load_pairs<D, BITS>(reinterpret_cast<const uint8_t*>(kb16), tid, kref);
+#pragma unroll
+                    for (int e = 0; e < 2 * KT; e++) dkb[e] = h2_sub(dkb[e], kref[e]);
+                }
                 uint32_t ka[KT][4];                                       // A fragments of this 16-token tile
                 k_frags<D, BITS>(codes + mtt * 16 * F::DC, koff, ks, dkb, ka);
 #pragma unroll
@@ -580,7 +604,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
         }
     // the tail page: exact K from tail_k, V rows from its record, fp32 on the CUDA cores; warp w takes heads w, w+NW..
     {
-        const bool has_tail = tail_n > 0 && z == n_splits - 1;
+        const bool has_tail = tail_n > 0 && sr.last;
         const IN* tk = has_tail ? tail_k + ((int64_t(tail_idx[s]) * H + h) * P + min(lane, P - 1)) * D : nullptr;
         const uint8_t* trec = has_tail ? hcache + int64_t(bt[full]) * block_stride : nullptr;
         constexpr int R = D / WARP;

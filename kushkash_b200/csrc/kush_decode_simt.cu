@@ -6,9 +6,9 @@
 // folds into q and the K bias into one scalar per head; V scales fold into the softmax weights and V biases into
 // one scalar per head; page-granular online softmax; the last n % P tokens take K from the exact tail.
 //
-// grid (S, Hkv, n_splits), block NW warps.  Split z owns a contiguous page range (kushkash/kush/gpu.mojo:418-424);
-// warp w takes pages start + w, start + w + NW, ...; the warp that would take the next page also takes the tail
-// (last split only).  Per page: lane t = token t for the QK dots (q' broadcast from shared memory), lane = output
+// grid (S, Hkv, n_splits), block NW warps.  Split z owns a contiguous page range (split_range: a quota of pages per
+// split for the whole batch); warp w takes pages start + w, start + w + NW, ...; the warp that would take the next
+// page also takes the tail (the last split with pages only).  Per page: lane t = token t for the QK dots (q' broadcast from shared memory), lane = output
 // dims for the PV accumulation (accumulators in shared memory, G*D floats per warp).
 #include "kush_common.cuh"
 
@@ -38,8 +38,16 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     const int64_t n = seq_lens[s];
     const int tail_n = int(n % P);
     const int64_t full = n / P;
-    const int64_t pps = (full + n_splits - 1) / n_splits;
-    const int64_t p0 = min(full, z * pps), p1 = min(full, p0 + pps);
+    const SplitRange sr = split_range(seq_lens, int(gridDim.x), s, z, n_splits, P);
+    if (!sr.active) {                                      // no pages here: an empty partial
+        for (int g = threadIdx.x; g < G; g += NW * WARP) {
+            const int64_t pb = ((int64_t(s) * H + h) * n_splits + z) * G + g;
+            part_ml[pb * 2] = -INFINITY;
+            part_ml[pb * 2 + 1] = 0.0f;
+        }
+        return;
+    }
+    const int64_t p0 = sr.p0, p1 = sr.p1;
     const int32_t* bt = block_table + s * max_pages;
     const int64_t qbase = (int64_t(s) * H + h) * G * D;
 
@@ -122,7 +130,7 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     }
     // tail page: last split, the warp that would take the next page (kushkash/kush/gpu.mojo:1001-1028)
     const int64_t npg = max(int64_t(0), p1 - p0);
-    if (tail_n > 0 && z == n_splits - 1 && wid == int(npg % NW)) {
+    if (tail_n > 0 && sr.last && wid == int(npg % NW)) {
         const IN* tk = tail_k + (int64_t(tail_idx[s]) * H + h) * P * D;
         const uint8_t* trec = cache + int64_t(bt[full]) * block_stride + int64_t(h) * head_stride;
         for (int g = 0; g < G; g++) {

@@ -125,6 +125,45 @@ def test_decode_split_kv(n_splits, P):
     assert_close(out, want, torch.bfloat16, f"splits={n_splits}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("n_splits", [1, 3, 8, 64])
+def test_decode_ragged_splits(n_splits, dtype):
+    """A ragged batch (0 tokens .. 200 pages, with and without tail pages) at split counts 1 to 64: the batch-wide
+    page quota leaves the short sequences' later splits empty and moves each tail to the last split with pages; the
+    outputs equal the oracle's at every split count (bf16: tensor-core kernel, fp32: CUDA-core kernel)."""
+    D, bits, G, P, H = 128, 4, 4, 16, 2
+    lens = [0, 1, 9, P, 3 * P + 5, 40 * P + 7, 200 * P, 17 * P + 15, 64 * P + 1]
+    B = len(lens)
+    pages = max(-(-n // P) for n in lens)
+    g = torch.Generator().manual_seed(11)
+    bt = torch.randperm(B * pages, generator=g).to(torch.int32).view(B, pages)
+    T = sum(lens)
+    k = exact(torch.randn(T, H, D, generator=g) + 3 * torch.randn(H, D, generator=g), dtype)
+    v = exact(torch.randn(T, H, D, generator=g), dtype)
+    q = exact(torch.randn(B, H * G, D, generator=g), dtype)
+    qsl = torch.tensor([0] + lens, dtype=torch.int64).cumsum(0).to(torch.int32)
+    jobs = [(s, p) for s in range(B) for p in range(-(-lens[s] // P))]
+    js = torch.tensor([j[0] for j in jobs], dtype=torch.int32)
+    jp = torch.tensor([j[1] for j in jobs], dtype=torch.int32)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    ro, go = OracleOps(D, bits, G, P), gpu_ops(D, bits, G, dtype, P)
+    ref = make_state(B, H, D, bits, P, bt, B * pages)
+    st = make_state(B, H, D, bits, P, bt, B * pages, "cuda", dtype)
+    ref.seq_lens.copy_(sl)
+    st.seq_lens.copy_(sl.cuda())
+    ro.write(k, v, qsl, ref.seq_lens, ref.tail_idx, js, jp, ref.pool, ref.block_table, ref.tail_k)
+    go.write(k.to("cuda", dtype), v.to("cuda", dtype), qsl.cuda(), st.seq_lens, st.tail_idx, js.cuda(), jp.cuda(),
+             st.pool, st.block_table, st.tail_k)
+    assert torch.equal(st.pool.cpu(), ref.pool)
+    want = torch.empty(B, H * G, D)
+    ro.decode(q.contiguous(), want, ref.pool, ref.block_table, ref.seq_lens, ref.tail_idx, ref.tail_k, D ** -0.5)
+    out = torch.full((B, H * G, D), float("nan"), dtype=dtype, device="cuda")
+    work = torch.full((go.work_size(B, H, n_splits),), float("nan"), device="cuda")
+    go.decode(q.to("cuda", dtype).contiguous(), out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k,
+              D ** -0.5, n_splits, work)
+    assert_close(out, want, dtype, f"ragged splits={n_splits}")
+
+
 def test_decode_tail_only_and_exact_page():
     for n in (1, 5, 31, 32, 33, 64):
         out, want, _ = decode_both(128, 4, 4, 32, 2, 2, n, torch.bfloat16)
@@ -147,9 +186,10 @@ def test_fwht_bit_exact(D, dtype):
     assert torch.equal(gpu_ops(D, 4, 1, dtype).fwht(xc, out=xc).cpu(), got)        # in place
 
 
-def unpack_case(D, bits, P, dtype, rot, new_pad=0):
+def unpack_case(D, bits, P, dtype, rot, new_pad=0, out_shift=0):
     """Oracle and GPU unpack of one seeded case; new_pad > 0 gives k_new / v_new rows a stride of H * D + new_pad
-    elements (views into wider buffers), which takes the element-wise copy of the new rows."""
+    elements (views into wider buffers), which takes the element-wise copy of the new rows; out_shift > 0 starts kp and
+    vp that many elements into their allocations (not 16-byte aligned: the element-wise kernel)."""
     c = unpack_inputs(D, bits, P)
     names = ("page_blk", "page_dst", "tail_blk", "tail_info", "tail_k", "k_new", "v_new", "new_dst")
     shape = (c["rows"], c["H"], D)
@@ -159,8 +199,8 @@ def unpack_case(D, bits, P, dtype, rot, new_pad=0):
     rk, rv = torch.full(shape, float("nan")), torch.full(shape, float("nan"))
     OracleOps(D, bits, 1, P).unpack(c["records"], *[args[n] for n in names], rk, rv, rot)
     # NaN-filled on the host so untouched rows carry the same NaN bit pattern as the reference's
-    kp = torch.full(shape, float("nan")).to(dtype).cuda()
-    vp = torch.full(shape, float("nan")).to(dtype).cuda()
+    n_out = c["rows"] * c["H"] * D
+    kp, vp = [torch.full((n_out + out_shift,), float("nan")).to(dtype).cuda()[out_shift:].view(shape) for _ in "kv"]
     gargs = [args[n].cuda().to(dtype) if n in ("tail_k", "k_new", "v_new") else args[n].cuda() for n in names]
     if new_pad:
         for i in (5, 6):
@@ -190,6 +230,19 @@ def test_unpack_bit_exact(D, bits, P, dtype, rot):
 def test_unpack_strided_new_rows(pad, dtype):
     """New rows whose row stride is not a multiple of 16 bytes (pad 1, 3) and one that is (pad 8)."""
     kp, vp, rk, rv = unpack_case(128, 4, 16, dtype, False, new_pad=pad)
+    for got, want in ((kp.cpu(), rk.to(dtype)), (vp.cpu(), rv.to(dtype))):
+        a = got.view(torch.int16) if dtype != torch.float32 else got.view(torch.int32)
+        b = want.view(torch.int16) if dtype != torch.float32 else want.view(torch.int32)
+        assert torch.equal(a, b), f"{(a != b).sum().item()} of {a.numel()} values differ"
+
+
+@pytest.mark.parametrize("rot", [False, True])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("D,bits,P", [(128, 4, 16), (64, 8, 32)])
+def test_unpack_unaligned_output(D, bits, P, dtype, rot):
+    """kp / vp one element off a 16-byte boundary: the element-wise kernel, same bits."""
+    kp, vp, rk, rv = unpack_case(D, bits, P, dtype, rot, out_shift=1)
+    assert kp.data_ptr() % 16 != 0
     for got, want in ((kp.cpu(), rk.to(dtype)), (vp.cpu(), rv.to(dtype))):
         a = got.view(torch.int16) if dtype != torch.float32 else got.view(torch.int32)
         b = want.view(torch.int16) if dtype != torch.float32 else want.view(torch.int32)
