@@ -55,7 +55,9 @@ __global__ void __launch_bounds__(128) fwht_kernel(const IN* x, IN* y, int64_t x
 }
 
 // grid (n_pages + n_tail + ceil(n_new / 32), Hkv), block 128 (kushkash/kush/gpu.mojo:303-375 kush_unpack).
-// Block x < n_pages: history page; < n_pages + n_tail: partial page; else 32 rows of the new chunk.
+// Block x < n_pages: history page; < n_pages + n_tail: partial page; else 32 rows of the new chunk.  Element-wise
+// loads and stores: the form for records, tail slots or outputs that are not 16-byte aligned (unpack_vec_kernel
+// below takes every aligned call).
 template <int D, int BITS, int P, class IN>
 __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t* __restrict__ cache, int64_t block_stride,
                                                      int64_t head_stride, int H, const int32_t* __restrict__ page_blk,
@@ -121,13 +123,14 @@ __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t* __restrict__
     }
 }
 
-// ------------------------------------------------------------------ vectorised unpack (no rotation)
-// The form both reference callers launch (rot=False: kushkash/vllm/backend.py:848, kushkash/sglang/backend.py:376).
-// One warp per item: a (history page, kv head), a (partial page, kv head) or one new row (all kv heads).  Codes are
-// read 8 bytes at a time (a chunk: 8 channels for int8; 8 + 8 for int4, byte j holding channel j in its low nibble and
-// channel j + D/2 in its high one), dequantized as fma(code, scale, bias) in fp32, rounded once and written with
-// 16-byte stores.  Chunk c of a page is token c / NG, bytes 8 (c % NG) .. + 7 (NG = row bytes / 8, which divides 32);
-// lane l takes chunks l, l + 32, ..., so its channels -- and its K scales -- stay fixed over the page.
+// ------------------------------------------------------------------ vectorised unpack
+// Both reference callers launch the unrotated form (rot=False: kushkash/vllm/backend.py:848,
+// kushkash/sglang/backend.py:376); the rotate-back runs on the same layout (fwht_chunk).  One warp per item: a
+// (history page, kv head), a (partial page, kv head) or one new row (all kv heads).  Codes are read 8 bytes at a time
+// (a chunk: 8 channels for int8; 8 + 8 for int4, byte j holding channel j in its low nibble and channel j + D/2 in its
+// high one), dequantized as fma(code, scale, bias) in fp32, rounded once and written with 16-byte stores.  Chunk c
+// of a page is token c / NG, bytes 8 (c % NG) .. + 7 (NG = row bytes / 8, which divides 32); lane l takes chunks
+// l, l + 32, ..., so its channels -- and its K scales -- stay fixed over the page.
 //
 // Codes to fp32 without a conversion instruction: a byte u placed under the exponent of 2^23 (PRMT with 0x4B000000)
 // is the float 2^23 + u, and subtracting 2^23 + OFFS gives u - OFFS exactly.  The stored codes are two's complement;
@@ -246,6 +249,129 @@ __device__ __forceinline__ void unpack_page_vec(const uint8_t* __restrict__ rec,
     }
 }
 
+// Rotate-back on the chunk layout.  A token row is held by the NG lanes of one group; a lane holds channels
+// c0..c0+7 in lo and, for int4, D/2+c0..D/2+c0+7 in hi (c0 = 8 (lane % NG)).  The canonical butterflies, strides 1, 2,
+// ..., D/2 in that order: strides 1-4 inside lo / hi, strides 8 .. (the lanes' span) / 2 between lanes (shuffle xor
+// stride / 8), and for int4 stride D/2 between lo and hi; then the separately rounded multiply by fp32 1/sqrt(D).
+// Every value goes through the same correctly rounded operations as in fwht_warp, so the results are identical.
+template <int D, int BITS>
+__device__ __forceinline__ void fwht_chunk(float (&lo)[8], float (&hi)[8], int g) {
+    constexpr int NG = (BITS == 8 ? D : D / 2) / 8;
+    auto inreg = [](float (&y)[8]) {
+#pragma unroll
+        for (int h = 1; h < 8; h <<= 1)
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (!(k & h)) {
+                    const float a = y[k], b = y[k + h];
+                    y[k] = __fadd_rn(a, b);
+                    y[k + h] = __fsub_rn(a, b);
+                }
+    };
+    inreg(lo);
+    if constexpr (BITS == 4) inreg(hi);
+#pragma unroll
+    for (int m = 1; m < NG; m <<= 1) {
+        const bool upper = g & m;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float o = __shfl_xor_sync(0xffffffffu, lo[k], m);
+            lo[k] = upper ? __fsub_rn(o, lo[k]) : __fadd_rn(lo[k], o);
+            if constexpr (BITS == 4) {
+                const float oh = __shfl_xor_sync(0xffffffffu, hi[k], m);
+                hi[k] = upper ? __fsub_rn(oh, hi[k]) : __fadd_rn(hi[k], oh);
+            }
+        }
+    }
+    if constexpr (BITS == 4) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const float a = lo[k], b = hi[k];
+            lo[k] = __fadd_rn(a, b);
+            hi[k] = __fsub_rn(a, b);
+        }
+    }
+    const float sc = D == 64 ? __uint_as_float(0x3E000000u) : D == 128 ? __uint_as_float(0x3DB504F3u)
+                                                                        : __uint_as_float(0x3D800000u);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        lo[k] = __fmul_rn(lo[k], sc);
+        hi[k] = __fmul_rn(hi[k], sc);
+    }
+}
+
+template <int BITS>
+__device__ __forceinline__ void chunk_vals(uint2 w, const float (&s0)[8], const float (&b0)[8], const float (&s1)[8],
+                                           const float (&b1)[8], float (&lo)[8], float (&hi)[8]) {
+    if constexpr (BITS == 4) {
+        deq8<8>((w.x & 0x0F0F0F0Fu) ^ 0x08080808u, (w.y & 0x0F0F0F0Fu) ^ 0x08080808u, s0, b0, lo);
+        deq8<8>(((w.x >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, ((w.y >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, s1, b1, hi);
+    } else {
+        deq8<128>(w.x ^ 0x80808080u, w.y ^ 0x80808080u, s0, b0, lo);
+#pragma unroll
+        for (int k = 0; k < 8; k++) hi[k] = 0.0f;
+    }
+}
+
+template <class IN>
+__device__ __forceinline__ void load8(const IN* p, float (&f)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) f[k] = to_f32(p[k]);
+}
+
+// unpack_page_vec with the rotate-back: every lane computes all P rows (rows n.. of a partial page are in bounds
+// and keep the shuffles convergent) and stores rows < n
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void unpack_page_vec_rot(const uint8_t* __restrict__ rec, const IN* __restrict__ tk, int n,
+                                                    IN* __restrict__ kout, IN* __restrict__ vout, int64_t rs,
+                                                    int lane) {
+    using F = Fmt<D, BITS, P>;
+    constexpr int NG = F::DC / 8, TPW = WARP / NG, PASSES = P / TPW;
+    const int g = lane % NG, t0 = lane / NG, c0 = 8 * g;
+    float s0[8], b0[8], s1[8], b1[8];
+    if (tk == nullptr) {
+        halves8(rec + F::OFF_KS + 2 * c0, s0);
+        halves8(rec + F::OFF_KB + 2 * c0, b0);
+        if constexpr (BITS == 4) {
+            halves8(rec + F::OFF_KS + 2 * (c0 + D / 2), s1);
+            halves8(rec + F::OFF_KB + 2 * (c0 + D / 2), b1);
+        }
+    }
+#pragma unroll 1
+    for (int i = 0; i < PASSES; i++) {
+        const int t = t0 + TPW * i;
+        float lo[8], hi[8];
+        if (tk == nullptr) {
+            chunk_vals<BITS>(__ldg(reinterpret_cast<const uint2*>(rec + t * F::DC + c0)), s0, b0, s1, b1, lo, hi);
+        } else {
+            load8(tk + t * D + c0, lo);
+            if constexpr (BITS == 4) load8(tk + t * D + D / 2 + c0, hi);
+            else
+#pragma unroll
+                for (int k = 0; k < 8; k++) hi[k] = 0.0f;
+        }
+        fwht_chunk<D, BITS>(lo, hi, g);
+        if (t < n) {
+            store8<IN>(kout + t * rs + c0, lo);
+            if constexpr (BITS == 4) store8<IN>(kout + t * rs + D / 2 + c0, hi);
+        }
+    }
+#pragma unroll 1
+    for (int i = 0; i < PASSES; i++) {
+        const int t = t0 + TPW * i;
+        float s[8], b[8], lo[8], hi[8];
+        const float vsc = h_load(rec + F::OFF_VS, t), vbi = h_load(rec + F::OFF_VB, t);
+#pragma unroll
+        for (int k = 0; k < 8; k++) s[k] = vsc, b[k] = vbi;
+        chunk_vals<BITS>(__ldg(reinterpret_cast<const uint2*>(rec + F::OFF_VQ + t * F::DC + c0)), s, b, s, b, lo, hi);
+        fwht_chunk<D, BITS>(lo, hi, g);
+        if (t < n) {
+            store8<IN>(vout + t * rs + c0, lo);
+            if constexpr (BITS == 4) store8<IN>(vout + t * rs + D / 2 + c0, hi);
+        }
+    }
+}
+
 // grid (ceil(warps / 8)), block 256; warps = (n_pages + n_tail) * H + n_new.  Records, tail_k, kp and vp 16-byte
 // aligned (the host checks); vec_new: k_new / v_new rows 16-byte aligned, else the new rows are copied by element.
 template <int D, int BITS, int P, class IN>
@@ -254,7 +380,7 @@ __global__ void __launch_bounds__(256) unpack_vec_kernel(
     const int32_t* __restrict__ page_blk, const int32_t* __restrict__ page_dst, int n_pages,
     const int32_t* __restrict__ tail_blk, const int32_t* __restrict__ tail_info, int n_tail,
     const IN* __restrict__ tail_k, const IN* __restrict__ k_new, const IN* __restrict__ v_new, int64_t ks, int64_t vs,
-    const int32_t* __restrict__ new_dst, int n_new, IN* __restrict__ kp, IN* __restrict__ vp, int vec_new) {
+    const int32_t* __restrict__ new_dst, int n_new, IN* __restrict__ kp, IN* __restrict__ vp, int vec_new, int rot) {
     const int lane = threadIdx.x % WARP;
     const int64_t wi = int64_t(blockIdx.x) * (blockDim.x / WARP) + threadIdx.x / WARP;
     const int64_t rs = int64_t(H) * D;
@@ -267,8 +393,12 @@ __global__ void __launch_bounds__(256) unpack_vec_kernel(
         const int64_t dst0 = page ? page_dst[i] : tail_info[3 * i];
         const int n = page ? P : tail_info[3 * i + 1];
         const IN* tk = page ? nullptr : tail_k + (int64_t(tail_info[3 * i + 2]) * H + h) * P * D;
-        unpack_page_vec<D, BITS, P, IN>(rec, tk, n, kp + dst0 * rs + int64_t(h) * D, vp + dst0 * rs + int64_t(h) * D,
-                                        rs, lane);
+        IN* kout = kp + dst0 * rs + int64_t(h) * D;
+        IN* vout = vp + dst0 * rs + int64_t(h) * D;
+        if (rot)
+            unpack_page_vec_rot<D, BITS, P, IN>(rec, tk, n, kout, vout, rs, lane);
+        else
+            unpack_page_vec<D, BITS, P, IN>(rec, tk, n, kout, vout, rs, lane);
     } else if (wi < n_pw + n_tw + n_new) {
         const int64_t j = wi - n_pw - n_tw;
         const int64_t o = int64_t(new_dst[j]) * rs;
@@ -325,7 +455,7 @@ extern "C" int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, i
     int rc = dispatch_fmt(head_dim, bits, page, dtype, [&](auto D, auto B, auto P, auto in) {
         using IN = decltype(in);
         const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-        const bool vec = !rot && a16(cache) && block_stride % 16 == 0 && head_stride % 16 == 0 && a16(kp) && a16(vp) &&
+        const bool vec = a16(cache) && block_stride % 16 == 0 && head_stride % 16 == 0 && a16(kp) && a16(vp) &&
                          (n_tail == 0 || a16(tail_k));
         if (vec) {
             const int64_t es = int64_t(sizeof(IN));
@@ -337,7 +467,7 @@ extern "C" int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, i
                     static_cast<const uint8_t*>(cache), block_stride, head_stride, hkv, page_blk, page_dst, n_pages,
                     tail_blk, tail_info, n_tail, static_cast<const IN*>(tail_k), static_cast<const IN*>(k_new),
                     static_cast<const IN*>(v_new), k_stride, v_stride, new_dst, n_new, static_cast<IN*>(kp),
-                    static_cast<IN*>(vp), vec_new);
+                    static_cast<IN*>(vp), vec_new, rot);
             return check_launch("kush_sm100_unpack");
         }
         dim3 grid(unsigned(blocks), hkv);
