@@ -333,6 +333,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="config 4 on N > 1 GPUs: outputs gathered by the combine's stores into every rank's buffer "
+                         "over NVLink (one CUDA graph per step) or by an NCCL all_gather per layer (eager steps)")
     ap.add_argument("--workload", choices=["batch", "long", "mix", "c1", "c2", "unpack"], default="batch",
                     help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned); "
                          "mix: config 5 (serving mix); c1, c2: configs 1 and 2 (single layer; requests partitioned); "
@@ -500,7 +503,7 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     """4 sequences of 131072 tokens; rank r owns kv heads [8r/N, 8(r+1)/N) of every sequence and
     layer, runs append + split-KV decode for them, and the per-layer [4, 32/N, 128] outputs are all_gathered over NCCL
     (the only collective).  Strong scaling: the total work is fixed as N grows."""
-    from kushkash_b200.shard import gather_heads, kv_head_range
+    from kushkash_b200.shard import PeerGather, decode_gathered, gather_heads, kv_head_range
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -511,12 +514,24 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     geo = Geometry(a, hkv=h1 - h0)
     full = Geometry(a, hkv=8)
     eng = Engine(geo, dev, seed=4321 + rank, extra_tokens=a.warmup + a.steps + 8)
-    outs = [torch.empty(geo.B, full.HQ, geo.D, dtype=torch.bfloat16, device=dev) for _ in range(geo.L)]
+    pg = None
+    if dist is not None and a.gather == "peer":                 # gathered by the combine's peer stores
+        if eng.ns < 2:
+            eng.ns = 2
+            eng.work = torch.empty(eng.ops.work_size(geo.B, geo.HKV, 2), device=dev)
+        pg = PeerGather(geo.B, full.HQ, geo.D, torch.bfloat16, slots=geo.L)
+        outs = pg.outs
+    else:
+        outs = [torch.empty(geo.B, full.HQ, geo.D, dtype=torch.bfloat16, device=dev) for _ in range(geo.L)]
 
     def step():
         for layer in range(geo.L):
             eng.ops.append(eng.k_new[layer], eng.v_new[layer], eng.seq_lens[layer], eng.tail_idx, eng.pool[layer],
                            eng.block_table, eng.tail_k[layer], pos_offset=0, advance=True)
+            if pg is not None:
+                decode_gathered(eng.ops, eng.q[layer], eng.pool[layer], eng.block_table, eng.seq_lens[layer],
+                                eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work, pg, layer)
+                continue
             eng.ops.decode(eng.q[layer], eng.out[layer], eng.pool[layer], eng.block_table, eng.seq_lens[layer],
                            eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work)
             outs[layer].copy_(gather_heads(eng.out[layer]) if dist is not None else eng.out[layer])
@@ -529,10 +544,10 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     for _ in range(a.warmup - 1):
         step()
     graph = None
-    if dist is None:                            # one GPU: the whole step as one CUDA graph
+    if dist is None or pg is not None:          # the whole step as one CUDA graph (no library collective in it)
         graph = capture(step, dev)
         run = graph.replay
-    else:                                       # collectives are not captured: eager steps, NCCL gathers in between
+    else:                                       # NCCL collectives are never captured: eager steps
         run = step
         step()
     n0 = int(eng.seq_lens[0, 0].item())
@@ -560,13 +575,18 @@ def run_long(a, world: int, rank: int, local: int) -> None:
             "warmup": a.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
             "data": "synthetic (seeded bf16 N(0,1) K/V/q with per-channel key offsets N(0, 2), BASELINE config 4 shapes)",
-            "config": {**full.describe(), "parallelism": f"kv heads partitioned over {world} GPU(s), all_gather of "
-                       "outputs per layer", "n_splits": eng.ns},
+            "config": {**full.describe(), "parallelism": f"kv heads partitioned over {world} GPU(s), outputs "
+                       "gathered per layer " + ("by the split-KV combine's stores into every rank's buffer over "
+                       "NVLink (CUDA IPC), one wait kernel per layer" if pg is not None else
+                       "by an NCCL all_gather" if dist is not None else "(one GPU: none)"), "n_splits": eng.ns},
             "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "us_per_layer_step": round(ms_step * 1e3 / geo.L, 2),
             "decode_tokens_per_s": round(geo.B / (ms_step / 1e3), 1), "clocks": clocks,
-            "gpu_launches": a.steps * eng.launches_per_step(), "cuda_graph": graph is not None}), flush=True)
+            "gpu_launches": a.steps * (eng.launches_per_step() + (geo.L if pg is not None else 0)),
+            "cuda_graph": graph is not None}), flush=True)
     del graph, eng
+    if pg is not None:
+        pg.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -107,9 +107,10 @@ int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void *out
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);
 
-/* Bounded-wait watchdog of the kernels that wait on bulk copies: bit 0 set if a decode launch gave up waiting for a
- * page copy (its outputs were written as NaN), bit 1 if a bulk write gave up waiting for its input rows (the
- * records of that warp's remaining items were not written); 0 if neither.  clear != 0 resets both flags.
+/* Bounded-wait watchdog of the kernels that wait: bit 0 set if a decode launch gave up waiting for a page copy (its
+ * outputs were written as NaN), bit 1 if a bulk write gave up waiting for its input rows (the records of that
+ * warp's remaining items were not written), bit 2 if a peer-gather wait gave up on a peer (kush_sm100_gather_wait:
+ * the gathered outputs are incomplete); 0 if none.  clear != 0 resets the flags.
  * Synchronous (reads device variables); -1 on a CUDA error.  No counterpart in the reference, whose kernels have
  * no bounded waits. */
 int kush_sm100_device_error(int32_t clear);
@@ -140,6 +141,38 @@ int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
                       int32_t n_tail, const void *tail_k, const void *k_new, const void *v_new, int64_t k_stride,
                       int64_t v_stride, const int32_t *new_dst, int32_t n_new, void *kp, void *vp, int32_t rot,
                       void *stream);
+
+/* ---- Output gather of KV-head sharding over peer memory (one process per GPU, CUDA IPC over NVLink).
+ * Replaces the library all_gather that follows the sharded decode (kushkash_b200/shard.py gather_heads; the
+ * reference has no multi-GPU path of its own, its tensor parallelism is vLLM's).  No counterpart in the reference. */
+
+#define KUSH_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc of `bytes`, zero-filled: memory other processes can map with kush_sm100_ipc_open.  Synchronous. */
+int kush_sm100_ipc_alloc(int64_t bytes, void **ptr);
+int kush_sm100_ipc_free(void *ptr);
+/* The KUSH_IPC_HANDLE_BYTES-byte handle of an allocation made by kush_sm100_ipc_alloc (cudaIpcGetMemHandle). */
+int kush_sm100_ipc_handle(const void *ptr, uint8_t *handle);
+/* Map a peer's allocation from its handle (cudaIpcOpenMemHandle, peer access enabled lazily); close unmaps it. */
+int kush_sm100_ipc_open(const uint8_t *handle, void **ptr);
+int kush_sm100_ipc_close(void *ptr);
+
+/* Split-KV combine of this rank's kv heads (as kush_sm100_combine) whose results are stored into every rank's
+ * gathered output: outs is a device array of `world` pointers, outs[r] = rank r's [n_seqs][hkv*world*group]
+ * [head_dim] buffer (this rank's own buffer at outs[rank]); this rank's heads land at q heads
+ * [rank*hkv*group, (rank+1)*hkv*group).  After the last store, ctr[1] (this rank's gather count) is incremented and
+ * written with release semantics to flags[r][rank] of every rank r (flags: device array of `world` pointers to each
+ * rank's [world] uint32 counts).  ctr ([2] uint32, zero-initialised, this rank's memory) also counts the launch's
+ * finished blocks.  Every rank must run the same sequence of gathers. */
+int kush_sm100_combine_gather(int32_t head_dim, int32_t dtype, int32_t group, void *const *outs, int32_t rank,
+                              int32_t world, const float *part_ml, const float *part_o, int32_t n_splits, int32_t hkv,
+                              int32_t n_seqs, uint32_t *const *flags, uint32_t *ctr, void *stream);
+
+/* One warp that waits until every rank's count in this rank's flags[world] has reached ctr[1] (this rank's own
+ * count, set by its kush_sm100_combine_gather earlier on `stream`): after it, the gathered output of that gather is
+ * complete for the kernels that follow on `stream`.  The wait gives up after 2 s and sets bit 2 of
+ * kush_sm100_device_error. */
+int kush_sm100_gather_wait(const uint32_t *flags, int32_t world, const uint32_t *ctr, void *stream);
 
 #ifdef __cplusplus
 }

@@ -42,6 +42,13 @@ SIGNATURES = {
     "kush_sm100_record_bytes": [_i32, _i32, _i32],
     "kush_sm100_device_error": [_i32],
     "kush_sm100_selfcheck": [_p],
+    "kush_sm100_ipc_alloc": [_i64, _p],
+    "kush_sm100_ipc_free": [_p],
+    "kush_sm100_ipc_handle": [_p, _p],
+    "kush_sm100_ipc_open": [_p, _p],
+    "kush_sm100_ipc_close": [_p],
+    "kush_sm100_combine_gather": [_i32, _i32, _i32, _p, _i32, _i32, _p, _p, _i32, _i32, _i32, _p, _p, _p],
+    "kush_sm100_gather_wait": [_p, _i32, _p, _p],
     "kush_sm100_last_error": [],
     "kush_sm100_version": [],
 }
@@ -81,7 +88,7 @@ def check(rc: int, what: str) -> None:
 
 def device_error(clear: bool = True) -> int:
     """Bounded-wait flags since the last clear: bit 0 a decode launch gave up (its outputs are NaN), bit 1 a bulk
-    write gave up (some of its records were not written); 0 if neither."""
+    write gave up (some of its records were not written), bit 2 a peer-gather wait gave up on a peer; 0 if none."""
     rc = lib().kush_sm100_device_error(int(clear))
     if rc < 0:
         raise RuntimeError("kush_sm100_device_error: CUDA error")
@@ -94,6 +101,38 @@ def selfcheck() -> tuple[int, int, int]:
     out = (ctypes.c_uint64 * 3)()
     check(lib().kush_sm100_selfcheck(out), "kush_sm100_selfcheck")
     return out[0], out[1], out[2]
+
+
+def ipc_alloc(nbytes: int) -> int:
+    """Device address of `nbytes` of zero-filled cudaMalloc memory that other processes can map."""
+    p = ctypes.c_void_p()
+    check(lib().kush_sm100_ipc_alloc(int(nbytes), ctypes.byref(p)), "kush_sm100_ipc_alloc")
+    return int(p.value)
+
+
+def ipc_free(ptr: int) -> None:
+    check(lib().kush_sm100_ipc_free(ptr), "kush_sm100_ipc_free")
+
+
+def ipc_handle(ptr: int) -> bytes:
+    """The CUDA IPC handle (64 bytes) of an ipc_alloc allocation."""
+    buf = (ctypes.c_uint8 * 64)()
+    check(lib().kush_sm100_ipc_handle(ptr, buf), "kush_sm100_ipc_handle")
+    return bytes(buf)
+
+
+def ipc_open(handle: bytes) -> int:
+    """This process's address of a peer's allocation, from its handle."""
+    if len(handle) != 64:
+        raise ValueError("an IPC handle has 64 bytes")
+    p = ctypes.c_void_p()
+    check(lib().kush_sm100_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(handle), ctypes.byref(p)),
+          "kush_sm100_ipc_open")
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().kush_sm100_ipc_close(ptr), "kush_sm100_ipc_close")
 
 
 def raw_stream(device: int) -> int:

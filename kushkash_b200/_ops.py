@@ -165,19 +165,42 @@ class Ops:
         """out[s] = attention of q[s] ([Hq, D]) over the seq_lens[s] cached tokens of sequence s
         (kushkash/_ops.py:191-213).  n_splits > 1 needs `work` (fp32, >= S*Hkv*n_splits*G*(D+2) elements)."""
         S, H = q.shape[0], tail_k.shape[1]
-        bs, hs = _byte_strides(cache)
         part_ml = part_o = 0
         if n_splits > 1:
-            nml = S * H * n_splits * self.G * 2
-            if work is None or work.dtype != torch.float32 or work.numel() < nml + S * H * n_splits * self.G * self.D:
-                raise ValueError(f"decode: n_splits={n_splits} needs an fp32 work buffer of "
-                                 f">= {self.work_size(S, H, n_splits)} elements")
-            part_ml, part_o = work.data_ptr(), work.data_ptr() + nml * 4
-        self.k["decode"]((S, H, n_splits), 32 * self.cfg.warps, q.data_ptr(), out.data_ptr(), cache.data_ptr(), bs, hs,
-                         tail_k.data_ptr(), tail_idx.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
-                         block_table.stride(0), H, float(scale), n_splits, part_ml, part_o)
+            part_ml, part_o = self._parts(S, H, n_splits, work)
+        self._decode(q, out.data_ptr(), cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, part_ml,
+                     part_o)
         if n_splits > 1:
             self.k["combine"]((S, H, 1), 256, out.data_ptr(), part_ml, part_o, n_splits, H)
+
+    def decode_partials(self, q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
+                        seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float,
+                        n_splits: int, work: torch.Tensor) -> tuple[int, int]:
+        """The split-KV decode without its combine (n_splits >= 2): the per-split partials (m, l and unnormalised
+        outputs) in `work`, for a combine that writes elsewhere -- the peer gather of KV-head sharding
+        (kushkash_b200.shard.PeerGather).  Returns the device addresses (part_ml, part_o) inside `work`.  No
+        counterpart in the reference."""
+        if n_splits < 2:
+            raise ValueError("decode_partials needs n_splits >= 2")
+        S, H = q.shape[0], tail_k.shape[1]
+        part_ml, part_o = self._parts(S, H, n_splits, work)
+        self._decode(q, part_o, cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, part_ml, part_o)
+        return part_ml, part_o
+
+    def _parts(self, S: int, H: int, n_splits: int, work: torch.Tensor | None) -> tuple[int, int]:
+        nml = S * H * n_splits * self.G * 2
+        if work is None or work.dtype != torch.float32 or work.numel() < nml + S * H * n_splits * self.G * self.D:
+            raise ValueError(f"decode: n_splits={n_splits} needs an fp32 work buffer of "
+                             f">= {self.work_size(S, H, n_splits)} elements")
+        return work.data_ptr(), work.data_ptr() + nml * 4
+
+    def _decode(self, q, out_ptr: int, cache, block_table, seq_lens, tail_idx, tail_k, scale: float, n_splits: int,
+                part_ml: int, part_o: int) -> None:
+        S, H = q.shape[0], tail_k.shape[1]
+        bs, hs = _byte_strides(cache)
+        self.k["decode"]((S, H, n_splits), 32 * self.cfg.warps, q.data_ptr(), out_ptr, cache.data_ptr(), bs, hs,
+                         tail_k.data_ptr(), tail_idx.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
+                         block_table.stride(0), H, float(scale), n_splits, part_ml, part_o)
 
 
 # ---------------------------------------------------------------- format helpers (pure PyTorch, for tests / callers)

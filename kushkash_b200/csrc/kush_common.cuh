@@ -186,6 +186,7 @@ int check_launch(const char* what);
 
 // the streaming write's bounded-wait flag (1 if a wait gave up), optionally cleared; -1 on a CUDA error
 int write_error_flag(int clear);
+int gather_error_flag(int clear);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

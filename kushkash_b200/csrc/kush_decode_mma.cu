@@ -792,7 +792,7 @@ extern "C" int kush_sm100_device_error(int32_t clear) {
         const int zero = 0;
         cudaMemcpyToSymbol(kush::g_decode_error, &zero, sizeof(int));
     }
-    const int w = kush::write_error_flag(clear);
-    if (w < 0) return -1;
-    return (v ? 1 : 0) | (w ? 2 : 0);
+    const int w = kush::write_error_flag(clear), gt = kush::gather_error_flag(clear);
+    if (w < 0 || gt < 0) return -1;
+    return (v ? 1 : 0) | (w ? 2 : 0) | (gt ? 4 : 0);
 }
