@@ -173,15 +173,16 @@ class OverlappedIO:
     stream.  Every byte still crosses PCIe inside the timed region: the loop ends with the compute stream waiting for
     the copy stream."""
 
-    def __init__(self, inputs: dict[str, torch.Tensor], output: torch.Tensor, device: torch.device):
-        self.inputs, self.output, self.device = inputs, output, device
+    def __init__(self, inputs: dict[str, torch.Tensor], output, device: torch.device):
+        self.inputs, self.device = inputs, device
+        self.outputs = list(output) if isinstance(output, (list, tuple)) else [output]
         self.host_in = {k: v.cpu().pin_memory() for k, v in inputs.items()}
         self.stage_in = {k: torch.empty_like(v) for k, v in inputs.items()}
-        self.stage_out = torch.empty_like(output)
-        self.host_out = torch.empty(output.shape, dtype=output.dtype).pin_memory()
+        self.stage_out = [torch.empty_like(o) for o in self.outputs]
+        self.host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in self.outputs]
         self.copy_stream = torch.cuda.Stream(device)
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.host_in.values())
-        self.d2h_bytes = self.host_out.numel() * self.host_out.element_size()
+        self.d2h_bytes = sum(t.numel() * t.element_size() for t in self.host_out)
 
     def _prefetch(self, main) -> torch.cuda.Event:
         self.copy_stream.wait_stream(main)                  # the staging has been consumed
@@ -202,10 +203,12 @@ class OverlappedIO:
             compute()
             if out_done is not None:
                 main.wait_event(out_done)                   # the previous outputs have left the staging
-            self.stage_out.copy_(self.output)
+            for s, o in zip(self.stage_out, self.outputs):
+                s.copy_(o)
             self.copy_stream.wait_stream(main)
             with torch.cuda.stream(self.copy_stream):
-                self.host_out.copy_(self.stage_out, non_blocking=True)
+                for h, s in zip(self.host_out, self.stage_out):
+                    h.copy_(s, non_blocking=True)
             out_done = self.copy_stream.record_event()
         main.wait_stream(self.copy_stream)
 
@@ -573,7 +576,7 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     h0, h1 = kv_head_range(8, rank, world)
     geo = Geometry(a, hkv=h1 - h0)
     full = Geometry(a, hkv=8)
-    eng = Engine(geo, dev, seed=4321 + rank, extra_tokens=a.warmup + a.steps + 8)
+    eng = Engine(geo, dev, seed=4321 + rank, extra_tokens=a.warmup + 2 * a.steps + 8)
     pg = None
     if dist is not None and a.gather == "peer":                 # gathered by the combine's peer stores
         if eng.ns < 2:
@@ -623,10 +626,24 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     barrier()
     ms = e0.elapsed_time(e1)
     byts = sum(full.packed_bytes(n0 + i + 1) for i in range(a.steps)) * geo.L
+    # ---- e2e: q and the new K/V rows of every layer from pinned host memory, every layer's (gathered) outputs back,
+    # overlapped with the neighbouring steps (eager NCCL steps: copies around each step on the copy stream as well)
+    io = OverlappedIO({k: getattr(eng, k) for k in ("q", "k_new", "v_new")}, outs, dev)
+    io.run(1, run)
+    n_e2e = int(eng.seq_lens[0, 0].item())
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    io.run(a.steps, run)
+    x1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = x0.elapsed_time(x1)
+    e2e_byts = sum(full.packed_bytes(n_e2e + i + 1) for i in range(a.steps)) * geo.L
     if dist is not None:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, e2e_ms = (float(v) for v in t.tolist())
     if rank == 0:
         ms_step = ms / a.steps
         value = byts / (ms / 1e3) / 1e9
@@ -642,9 +659,12 @@ def run_long(a, world: int, rank: int, local: int) -> None:
             "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "us_per_layer_step": round(ms_step * 1e3 / geo.L, 2),
             "decode_tokens_per_s": round(geo.B / (ms_step / 1e3), 1), "clocks": clocks,
+            "e2e": {"value": round(e2e_byts / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": io.h2d_bytes, "d2h_bytes_per_step": io.d2h_bytes,
+                    "ms_per_step": round(e2e_ms / a.steps, 4)},
             "gpu_launches": a.steps * (eng.launches_per_step() + (geo.L if pg is not None else 0)),
             "cuda_graph": graph is not None}), flush=True)
-    del graph, eng
+    del graph, eng, io
     if pg is not None:
         pg.close()
     if dist is not None:
