@@ -70,7 +70,9 @@ def test_split_factor():
     from kushkash_b200._ops import split_factor
     assert split_factor(256, 8, 256, 148) == 1                    # 2048 units fill the GPU
     assert split_factor(4, 8, 4096, 148) == 18                    # config 4, one GPU: 32 units x 18 = 576 CTAs
-    assert split_factor(4, 1, 4096, 148) == 148                   # config 4, one kv head per GPU
+    assert split_factor(4, 4, 4096, 148) == 37                    # config 4 over 2 GPUs: 16 units x 37 = 592 CTAs
+    assert split_factor(4, 2, 4096, 148) == 41                    # over 4 GPUs: ~100-page splits, >= 2 CTAs per SM
+    assert split_factor(4, 1, 4096, 148) == 74                    # over 8 GPUs: 2 CTAs per SM
     assert split_factor(1, 1, 7, 148) == 1                        # too few pages to split
     assert split_factor(1, 1, 16, 148) == 1                       # >= 16 pages per split
     assert split_factor(1, 1, 64, 148) == 4
