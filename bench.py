@@ -467,8 +467,8 @@ def main() -> None:
         torch.cuda.synchronize(dev)
 
     # ---- timed region: K graph replays of the full step
+    sampler = ClockSampler(local)               # started before the barrier: its spawn cannot skew the ranks
     barrier()
-    sampler = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):
@@ -614,8 +614,8 @@ def run_long(a, world: int, rank: int, local: int) -> None:
         run = step
         step()
     n0 = int(eng.seq_lens[0, 0].item())
+    sampler = ClockSampler(local)               # started before the barrier: its spawn cannot skew the ranks
     barrier()
-    sampler = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):
@@ -988,8 +988,8 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
         eng.step()
     graph = capture(eng.step, dev)
     n_done = a.warmup - 1
+    sampler = ClockSampler(local)               # started before the barrier: its spawn cannot skew the ranks
     barrier()
-    sampler = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):
@@ -1266,8 +1266,8 @@ def run_unpack(a, world: int, rank: int, local: int) -> None:
         eng.step()
     graph = capture(eng.step, dev)
     graph.replay()
+    sampler = ClockSampler(local)               # started before the barrier: its spawn cannot skew the ranks
     barrier()
-    sampler = ClockSampler(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):
