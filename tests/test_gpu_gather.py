@@ -1,7 +1,8 @@
 """GPU tests of the peer-memory output gather of KV-head sharding (kushkash_b200.shard.PeerGather).
 
 One GPU: the gather of a single rank equals Ops.decode bit for bit (the same combine arithmetic), several slots
-keep their own outputs, and the gather count advances once per gather with no wait giving up.  Two GPUs (skipped
+keep their own outputs, and the gather count advances once per gather with no wait giving up; a wait on a peer
+that never gathers gives up after its limit and reports (failure detection without a fault).  Two GPUs (skipped
 with fewer): each of two processes decodes half of the kv heads, and every rank's gathered [S, Hq, D] output equals
 the unsharded decode bit for bit, eagerly and replayed from one CUDA graph."""
 import multiprocessing as mp
@@ -141,3 +142,26 @@ def test_two_rank_gather_equals_unsharded_decode():
                 p.kill()
     for r in range(2):
         assert results.get(r) == [True, True, True], f"rank {r}: {results.get(r)}"
+
+
+def test_gather_wait_gives_up_and_reports():
+    """A wait for a peer that never gathers (world 2 on a one-rank buffer: rank 1's count stays 0) gives up after
+    its limit (2 s) instead of hanging, sets bit 2 of device_error, and leaves the context usable."""
+    import time
+    from kushkash_b200 import _cuda
+    from kushkash_b200.shard import PeerGather
+    pg = PeerGather(1, 4, 64, torch.bfloat16, slots=1)
+    try:
+        _cuda.device_error(clear=True)
+        pg.count[1] = 1                                            # this rank has made one gather
+        t0 = time.monotonic()
+        _cuda.check(_cuda.lib().kush_sm100_gather_wait(pg.base + pg.flags_off, 2, pg.base + pg.ctr_off,
+                                                        _cuda.raw_stream(pg.device.index)), "gather_wait")
+        torch.cuda.synchronize()
+        waited = time.monotonic() - t0
+        assert 1.5 < waited < 30, waited
+        assert _cuda.device_error(clear=True) == 4
+        x = torch.ones(4, device="cuda")                           # the context still works
+        assert float((x * 2).sum()) == 8.0
+    finally:
+        pg.close()
