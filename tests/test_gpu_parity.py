@@ -110,6 +110,21 @@ def test_decode_matches_oracle(D, bits, G, P, B, H, n, dtype):
     assert_close(out, want, dtype, f"decode {D} {bits} {G} {P} {n}")
 
 
+# kernel instantiations the golden-pinned cases above do not reach: D 256 int4 at pages 16 (G 8) and 32 (G 4), two
+# n-tiles (G 12, 16) at int8 page 16 and D 64 page 32, one head per group at int8 page 16; each also split 3 ways
+MORE_DECODE_CASES = [(256, 4, 8, 16, 1, 2, 70), (128, 8, 12, 16, 1, 2, 50), (64, 4, 16, 32, 1, 1, 40),
+                     (128, 8, 1, 16, 2, 2, 33), (256, 4, 4, 32, 1, 2, 99)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D,bits,G,P,B,H,n", MORE_DECODE_CASES)
+def test_decode_more_instantiations(D, bits, G, P, B, H, n, dtype):
+    out, want, _ = decode_both(D, bits, G, P, B, H, n, dtype)
+    assert_close(out, want, dtype, f"decode {D} {bits} {G} {P} {n}")
+    out, want, _ = decode_both(D, bits, G, P, B, H, n, dtype, n_splits=3)
+    assert_close(out, want, dtype, f"decode {D} {bits} {G} {P} {n} splits 3")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("G", [1, 4, 7, 8, 12])
 def test_decode_gqa_groups(G, dtype):
