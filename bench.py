@@ -96,9 +96,9 @@ def key_offsets(geo: Geometry, gen: torch.Generator, device) -> torch.Tensor:
 class Engine:
     """32 layers of cache state on one GPU, filled with the context, plus the per-step inputs."""
 
-    def __init__(self, geo: Geometry, device: torch.device, seed: int, extra_tokens: int):
+    def __init__(self, geo: Geometry, device: torch.device, seed: int, extra_tokens: int, rotate: str = "none"):
         from kushkash_b200 import Ops
-        self.geo, self.dev = geo, device
+        self.geo, self.dev, self.rotate = geo, device, rotate
         g = geo
         self.ops = Ops(device, g.D, g.bits, g.G, torch.bfloat16, g.P)
         gen = torch.Generator().manual_seed(seed)
@@ -122,6 +122,7 @@ class Engine:
         self.v_new = torch.randn(g.L, g.B, g.HKV, g.D, generator=dgen, device=device).to(torch.bfloat16)
         self.q = torch.randn(g.L, g.B, g.HQ, g.D, generator=dgen, device=device).to(torch.bfloat16)
         self.out = torch.empty_like(self.q)
+        self.set_rotation(rotate)
 
     def _keys(self, x: torch.Tensor) -> torch.Tensor:
         return x + self.offsets.to(x.dtype)
@@ -136,6 +137,8 @@ class Engine:
                 T = min(chunk, g.N - n)
                 k = self._keys(torch.randn(g.B, T, g.HKV, g.D, generator=dgen, device=self.dev)).to(torch.bfloat16)
                 v = torch.randn(g.B, T, g.HKV, g.D, generator=dgen, device=self.dev).to(torch.bfloat16)
+                if self.rotate != "none":       # a rotated cache holds K H and V H
+                    k, v = self.ops.fwht(k, out=k), self.ops.fwht(v, out=v)
                 self.seq_lens[layer].fill_(n + T)
                 pages = torch.arange(n // g.P, (n + T - 1) // g.P + 1, dtype=torch.int32, device=self.dev)
                 job_seq = torch.arange(g.B, dtype=torch.int32, device=self.dev).repeat_interleave(pages.numel())
@@ -146,23 +149,42 @@ class Engine:
                 n += T
         torch.cuda.synchronize(self.dev)
 
+    rotate = "none"         # "fused": rotation inside the append / decode kernels; "unfused": fwht launches around
+
     def step(self) -> None:
         """One decode step: per layer, append one token per sequence, then decode attention (2 launches/layer)."""
         g, ops = self.geo, self.ops
         for layer in range(g.L):
-            ops.append(self.k_new[layer], self.v_new[layer], self.seq_lens[layer], self.tail_idx, self.pool[layer],
-                       self.block_table, self.tail_k[layer], pos_offset=0, advance=True)
-            ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.block_table, self.seq_lens[layer],
-                       self.tail_idx, self.tail_k[layer], self.scale, self.ns, self.work)
+            k, v = self.k_new[layer], self.v_new[layer]
+            if self.rotate == "unfused":
+                k, v = ops.fwht(k, out=self.rk), ops.fwht(v, out=self.rv)
+            ops.append(k, v, self.seq_lens[layer], self.tail_idx, self.pool[layer], self.block_table,
+                       self.tail_k[layer], pos_offset=0, advance=True, rotate=self.rotate == "fused")
+            self._decode(layer)
+
+    def _decode(self, layer: int) -> None:
+        g, ops = self.geo, self.ops
+        q = ops.fwht(self.q[layer], out=self.rq) if self.rotate == "unfused" else self.q[layer]
+        ops.decode(q, self.out[layer], self.pool[layer], self.block_table, self.seq_lens[layer], self.tail_idx,
+                   self.tail_k[layer], self.scale, self.ns, self.work, rotate=self.rotate == "fused")
+        if self.rotate == "unfused":
+            ops.fwht(self.out[layer], out=self.out[layer])
+
+    def set_rotation(self, mode: str) -> None:
+        self.rotate = mode
+        if mode == "unfused":                   # scratch rows for the rotated k, v, q of a layer
+            self.rk, self.rv = torch.empty_like(self.k_new[0]), torch.empty_like(self.v_new[0])
+            self.rq = torch.empty_like(self.q[0])
 
     def decode_only(self) -> None:
+        """The decode launches alone (with rotation fused into them when it is on), for the kernel's roofline."""
         g, ops = self.geo, self.ops
         for layer in range(g.L):
             ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.block_table, self.seq_lens[layer],
-                       self.tail_idx, self.tail_k[layer], self.scale, self.ns, self.work)
+                       self.tail_idx, self.tail_k[layer], self.scale, self.ns, self.work, rotate=self.rotate == "fused")
 
     def launches_per_step(self) -> int:
-        return self.geo.L * (2 + (1 if self.ns > 1 else 0))
+        return self.geo.L * (2 + (1 if self.ns > 1 else 0) + (4 if self.rotate == "unfused" else 0))
 
 
 class OverlappedIO:
@@ -405,6 +427,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rotate", choices=["none", "fused", "unfused"], default="none",
+                    help="config 3 with the Walsh-Hadamard rotation of kushkash's 4-bit default: inside the append and "
+                         "decode kernels (fused) or as fwht launches around them (unfused); BASELINE runs without")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="config 4 on N > 1 GPUs: outputs gathered by the combine's stores into every rank's buffer "
                          "over NVLink (one CUDA graph per step) or by an NCCL all_gather per layer (eager steps)")
@@ -453,7 +478,7 @@ def main() -> None:
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    eng = Engine(geo, dev, seed=1234 + rank, extra_tokens=a.warmup + 2 * a.steps + 8)
+    eng = Engine(geo, dev, seed=1234 + rank, extra_tokens=a.warmup + 2 * a.steps + 8, rotate=a.rotate)
 
     # warm-up (eager, then capture the step)
     for _ in range(a.warmup - 1):
@@ -537,7 +562,10 @@ def main() -> None:
             "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
             "data": "synthetic (seeded bf16 N(0,1) K/V/q with per-channel key offsets, BASELINE config 3 shapes)",
             "config": {**geo.describe(), "global_batch": geo.B * world,
-                       "parallelism": f"requests partitioned over {world} GPU(s), no collective in the step"},
+                       "parallelism": f"requests partitioned over {world} GPU(s), no collective in the step",
+                       "rotation": {"none": "off (as BASELINE)", "fused": "Walsh-Hadamard inside the append and decode "
+                                    "kernels", "unfused": "Walsh-Hadamard by fwht launches around append and decode"}[
+                           a.rotate]},
             "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "us_per_layer_step": round(ms_step * 1e3 / geo.L, 2),
             "decode_tokens_per_s": round(geo.B * world / (ms_step / 1e3), 1),

@@ -103,6 +103,31 @@ int kush_sm100_decode_noalloc(int32_t head_dim, int32_t bits, int32_t page, int3
 int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void *out, const float *part_ml,
                        const float *part_o, int32_t n_splits, int32_t hkv, int32_t n_seqs, void *stream);
 
+/* ---- Rotation fused into the decode step with rotation on (kushkash's default at 4 bits),
+ * the reference rotates q, k, v and the output with cuBLAS GEMMs around its kernels (kushkash/_ops.py:489-518,
+ * cache.py:146-183).  These entry points take the unrotated rows and apply the canonical Walsh-Hadamard rotation
+ * (as kush_sm100_fwht) inside the kernels.  No counterpart kernels in the reference. */
+
+/* kush_sm100_append of rows k_new / v_new rotated first: pages and tail bit-identical to kush_sm100_fwht (rounded
+ * to dtype) followed by kush_sm100_append. */
+int kush_sm100_append_rotated(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void *k_new,
+                              const void *v_new, int64_t k_stride, int64_t v_stride, int32_t *seq_lens,
+                              int32_t pos_offset, int32_t advance, const int32_t *tail_idx, void *cache,
+                              int64_t block_stride, int64_t head_stride, void *tail_k, const int32_t *block_table,
+                              int64_t max_pages, int32_t hkv, int32_t n_seqs, void *stream);
+
+/* kush_sm100_decode over a rotated cache with an unrotated q: q is rotated in fp32 inside the kernel and the output
+ * rotated back before its store (n_splits == 1; with n_splits > 1 follow with kush_sm100_combine_rotated). */
+int kush_sm100_decode_rotated(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+                              const void *q, void *out, const void *cache, int64_t block_stride, int64_t head_stride,
+                              const void *tail_k, const int32_t *tail_idx, const int32_t *block_table,
+                              const int32_t *seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
+                              float *part_ml, float *part_o, int32_t n_seqs, void *stream);
+
+/* kush_sm100_combine with the merged output rotated back before its store. */
+int kush_sm100_combine_rotated(int32_t head_dim, int32_t dtype, int32_t group, void *out, const float *part_ml,
+                               const float *part_o, int32_t n_splits, int32_t hkv, int32_t n_seqs, void *stream);
+
 /* Which decode kernel a configuration takes: 1 = tensor-core kernel (mma), 0 = CUDA-core kernel,
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);

@@ -33,6 +33,11 @@ SIGNATURES = {
     "kush_sm100_decode": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32, _i32,
                           _p, _p, _i32, _p],
     "kush_sm100_combine": [_i32, _i32, _i32, _p, _p, _p, _i32, _i32, _i32, _p],
+    "kush_sm100_append_rotated": [_i32, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _i32, _i32, _p, _p, _i64, _i64, _p,
+                                  _p, _i64, _i32, _i32, _p],
+    "kush_sm100_decode_rotated": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,
+                                  _f32, _i32, _p, _p, _i32, _p],
+    "kush_sm100_combine_rotated": [_i32, _i32, _i32, _p, _p, _p, _i32, _i32, _i32, _p],
     "kush_sm100_decode_noalloc": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,
                                   _f32, _i32, _i32, _p],
     "kush_sm100_decode_tensor_cores": [_i32, _i32, _i32, _i32, _i32],
@@ -153,7 +158,7 @@ class Kernel:
     def __init__(self, device: int, cfg: GpuConfig, name: str):
         self.device, self.cfg, self.name = device, cfg, name
         self.fn = getattr(lib(), "kush_sm100_" + name)
-        self._call = getattr(self, "_" + name)
+        self._call = getattr(self, "_" + name.removesuffix("_rotated"))    # a rotated variant takes the same arguments
 
     def __call__(self, grid: tuple[int, int, int], block: int, *args) -> None:
         with torch.cuda.device(self.device):
@@ -202,7 +207,7 @@ class Kernel:
                        raw_stream(self.device))
 
 
-NAMES = ("append", "write", "decode", "combine", "fwht", "unpack")
+NAMES = ("append", "write", "decode", "combine", "fwht", "unpack", "append_rotated", "decode_rotated", "combine_rotated")
 
 
 @lru_cache(None)

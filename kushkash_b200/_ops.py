@@ -84,11 +84,13 @@ class Ops:
     # ---------------------------------------------------------------- writes
     def append(self, k: torch.Tensor, v: torch.Tensor, seq_lens: torch.Tensor, tail_idx: torch.Tensor,
                cache: torch.Tensor, block_table: torch.Tensor, tail_k: torch.Tensor,
-               pos_offset: int, advance: bool) -> None:
-        """One token per sequence: row s of k/v goes to position seq_lens[s] + pos_offset (kushkash/_ops.py:66-80)."""
+               pos_offset: int, advance: bool, *, rotate: bool = False) -> None:
+        """One token per sequence: row s of k/v goes to position seq_lens[s] + pos_offset (kushkash/_ops.py:66-80).
+        rotate=True (an extension): the rows are rotated (canonical Walsh-Hadamard) inside the kernel first, bit for
+        bit what fwht() then append() store."""
         S, H = k.shape[0], k.shape[1]
         bs, hs = _byte_strides(cache)
-        self.k["append"]((S, 1, 1), self.D, k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), seq_lens.data_ptr(),
+        self.k["append_rotated" if rotate else "append"]((S, 1, 1), self.D, k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), seq_lens.data_ptr(),
                          pos_offset, int(advance), tail_idx.data_ptr(), cache.data_ptr(), bs, hs,
                          tail_k.data_ptr(), block_table.data_ptr(), block_table.stride(0), H)
 
@@ -168,17 +170,20 @@ class Ops:
 
     def decode(self, q: torch.Tensor, out: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor,
-               scale: float, n_splits: int = 1, work: torch.Tensor | None = None) -> None:
+               scale: float, n_splits: int = 1, work: torch.Tensor | None = None, *, rotate: bool = False) -> None:
         """out[s] = attention of q[s] ([Hq, D]) over the seq_lens[s] cached tokens of sequence s
-        (kushkash/_ops.py:191-213).  n_splits > 1 needs `work` (fp32, >= S*Hkv*n_splits*G*(D+2) elements)."""
+        (kushkash/_ops.py:191-213).  n_splits > 1 needs `work` (fp32, >= S*Hkv*n_splits*G*(D+2) elements).
+        rotate=True (an extension, for a cache written with rotation): q is rotated inside the kernel and the output
+        rotated back before its store, in place of fwht(q) before and fwht(out) after."""
         S, H = q.shape[0], tail_k.shape[1]
         part_ml = part_o = 0
         if n_splits > 1:
             part_ml, part_o = self._parts(S, H, n_splits, work)
         self._decode(q, out.data_ptr(), cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, part_ml,
-                     part_o)
+                     part_o, rotate)
         if n_splits > 1:
-            self.k["combine"]((S, H, 1), 256, out.data_ptr(), part_ml, part_o, n_splits, H)
+            self.k["combine_rotated" if rotate else "combine"]((S, H, 1), 256, out.data_ptr(), part_ml, part_o,
+                                                               n_splits, H)
 
     def decode_partials(self, q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                         seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float,
@@ -202,10 +207,10 @@ class Ops:
         return work.data_ptr(), work.data_ptr() + nml * 4
 
     def _decode(self, q, out_ptr: int, cache, block_table, seq_lens, tail_idx, tail_k, scale: float, n_splits: int,
-                part_ml: int, part_o: int) -> None:
+                part_ml: int, part_o: int, rotate: bool = False) -> None:
         S, H = q.shape[0], tail_k.shape[1]
         bs, hs = _byte_strides(cache)
-        self.k["decode"]((S, H, n_splits), 32 * self.cfg.warps, q.data_ptr(), out_ptr, cache.data_ptr(), bs, hs,
+        self.k["decode_rotated" if rotate else "decode"]((S, H, n_splits), 32 * self.cfg.warps, q.data_ptr(), out_ptr, cache.data_ptr(), bs, hs,
                          tail_k.data_ptr(), tail_idx.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
                          block_table.stride(0), H, float(scale), n_splits, part_ml, part_o)
 

@@ -7,7 +7,9 @@ Memory per layer (kushkash/cache.py:6-12):
                                         final in the page's record
 Shared by all layers: block_table int32 [B, max_pages] (logical -> physical page).
 With rotation on (rotate=, KUSHKASH_ROTATE; default on at 4 bits), pages and tail hold K H and V H (canonical
-Walsh-Hadamard H, computed by the library's fwht kernel); every public method takes and returns unrotated tensors.
+Walsh-Hadamard H); every public method takes and returns unrotated tensors.  The decode step rotates inside its
+kernels (the rotated append, the decode that rotates q and its output); multi-token writes rotate with the fwht
+kernel first.
 `page` is the tokens per page record: 32 is kushkash's format, 16 the same layout with 16 rows.
 """
 from __future__ import annotations
@@ -135,12 +137,15 @@ class KushCache:
             return
         n, P = self._len[layer], self.P
         self._map(-(-(n + T) // P))
-        k = self._rotate(k).transpose(1, 2).contiguous().reshape(B * T, H, D)
-        v = self._rotate(v).transpose(1, 2).contiguous().reshape(B * T, H, D)
         args = dict(cache=self.pool[layer], block_table=self.block_table, tail_k=self.tail_k[layer])
-        if T == 1:
-            self.ops.append(k, v, self.seq_lens[layer], self.tail_idx, pos_offset=0, advance=True, **args)
+        if T == 1:                                  # rotation (if on) inside the append kernel
+            k = k.to(self.kdtype).reshape(B, H, D).contiguous()
+            v = v.to(self.kdtype).reshape(B, H, D).contiguous()
+            self.ops.append(k, v, self.seq_lens[layer], self.tail_idx, pos_offset=0, advance=True, rotate=self.rot,
+                            **args)
         else:
+            k = self._rotate(k).transpose(1, 2).contiguous().reshape(B * T, H, D)
+            v = self._rotate(v).transpose(1, 2).contiguous().reshape(B * T, H, D)
             self.seq_lens[layer].fill_(n + T)
             pages = torch.arange(n // P, (n + T - 1) // P + 1, dtype=torch.int32, device=self.device)
             job_seq = torch.arange(B, dtype=torch.int32, device=self.device).repeat_interleave(pages.numel())
@@ -153,7 +158,7 @@ class KushCache:
         (kushkash/cache.py:164-183)."""
         if self._len[layer] == 0:
             raise RuntimeError("attend() on an empty cache")
-        q = self._rotate(q)
+        q = q.to(self.kdtype).contiguous()                 # rotated (if on) inside the decode kernel
         out = torch.empty_like(q)
         ns = self._frozen_ns or self.ops.splits(self.B, self.H, self._len[layer] // self.P)
         if ns > 1:
@@ -161,8 +166,7 @@ class KushCache:
             if self._work.numel() < need:
                 self._work = torch.empty(need, dtype=torch.float32, device=self.device)
         self.ops.decode(q, out, self.pool[layer], self.block_table, self.seq_lens[layer], self.tail_idx,
-                        self.tail_k[layer], self.scale, ns, self._work)
-        out = self.ops.fwht(out) if self.rot else out
+                        self.tail_k[layer], self.scale, ns, self._work, rotate=self.rot)
         return out.to(self.dtype)
 
     def dequantize(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:

@@ -26,13 +26,13 @@ int check_launch(const char* what) {
 int launch_decode_simt_any(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
                            int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                            const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv,
-                           float scale, int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs,
+                           float scale, int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot,
                            cudaStream_t stream);
 int decode_mma_supported(int D, int bits, int P, int dtype, int G);
 int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
                       int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                       const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
-                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, cudaStream_t stream);
+                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, cudaStream_t stream);
 
 }  // namespace kush
 
@@ -56,11 +56,11 @@ extern "C" int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, in
     return decode_mma_supported(head_dim, bits, page, dtype, group) ? 1 : 0;
 }
 
-extern "C" int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+static int decode_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
                                  const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                                  const void* tail_k, const int32_t* tail_idx, const int32_t* block_table,
                                  const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
-                                 float* part_ml, float* part_o, int32_t n_seqs, void* stream) {
+                                 float* part_ml, float* part_o, int32_t n_seqs, int rot, void* stream) {
     if (n_seqs < 0 || hkv < 1 || group < 1 || n_splits < 1)
         return set_error(KUSH_ERR_ARG, "kush_sm100_decode: n_seqs %d hkv %d group %d n_splits %d", n_seqs, hkv, group,
                          n_splits);
@@ -79,13 +79,32 @@ extern "C" int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, i
     if (decode_mma_supported(head_dim, bits, page, dtype, group))
         return launch_decode_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
                                  tail_idx, block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o,
-                                 n_seqs, st);
+                                 n_seqs, rot, st);
     g_err[0] = 0;
     int rc = launch_decode_simt_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
                                     tail_idx, block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o,
-                                    n_seqs, st);
+                                    n_seqs, rot, st);
     if (rc == KUSH_ERR_UNSUPPORTED && g_err[0] == 0)
         return set_error(rc, "kush_sm100_decode: unsupported head_dim %d / bits %d / page %d / dtype %d", head_dim, bits,
                          page, dtype);
     return rc;
+}
+
+extern "C" int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+                                 const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
+                                 const void* tail_k, const int32_t* tail_idx, const int32_t* block_table,
+                                 const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
+                                 float* part_ml, float* part_o, int32_t n_seqs, void* stream) {
+    return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
+                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs, 0, stream);
+}
+
+extern "C" int kush_sm100_decode_rotated(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+                                         const void* q, void* out, const void* cache, int64_t block_stride,
+                                         int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
+                                         const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages,
+                                         int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
+                                         int32_t n_seqs, void* stream) {
+    return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
+                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs, 1, stream);
 }

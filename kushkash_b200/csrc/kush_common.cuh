@@ -109,6 +109,41 @@ __device__ __forceinline__ float warp_sum(float x) {
     return x;
 }
 
+// ------------------------------------------------------------------ canonical Walsh-Hadamard rotation of a row
+// A row of D values held by one warp, lane l holding y[i] = x[l + 32 i] (i < D/32).  The canonical order
+// (kushkash/kush/quant.mojo:90-122): fp32 butterflies over strides 1, 2, ..., D/2 in that order -- strides < 32 pair
+// lanes (shuffle xor), strides >= 32 pair a lane's own registers -- then one separately rounded multiply by fp32
+// 1/sqrt(D).  Adds, subtracts and the multiply are correctly rounded IEEE operations in a fixed order, so the result
+// equals the CPU's bit for bit.
+template <int D>
+__device__ __forceinline__ void fwht_warp(float (&y)[D / WARP], int lane) {
+    constexpr int R = D / WARP;
+#pragma unroll
+    for (int h = 1; h < WARP; h <<= 1) {                    // partner lane ^ h holds x[i ^ h]
+        const bool upper = lane & h;
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            const float other = __shfl_xor_sync(0xffffffffu, y[i], h);
+            y[i] = upper ? __fsub_rn(other, y[i]) : __fadd_rn(y[i], other);
+        }
+    }
+#pragma unroll
+    for (int hr = 1; hr < R; hr <<= 1) {                    // stride 32 * hr: register bit hr
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            if (!(i & hr)) {
+                const float a = y[i], b = y[i + hr];
+                y[i] = __fadd_rn(a, b);
+                y[i + hr] = __fsub_rn(a, b);
+            }
+        }
+    }
+    const float sc = D == 64 ? __uint_as_float(0x3E000000u) : D == 128 ? __uint_as_float(0x3DB504F3u)
+                                                                        : __uint_as_float(0x3D800000u);
+#pragma unroll
+    for (int i = 0; i < R; i++) y[i] = __fmul_rn(y[i], sc);
+}
+
 // ------------------------------------------------------------------ split-KV page ranges
 // The reference gives split z of a sequence with `full` full pages the range [z q, (z+1) q), q = ceil(full /
 // n_splits) (kushkash/kush/gpu.mojo:418-424): every sequence in n_splits pieces, however short.  Here the quota is

@@ -312,8 +312,9 @@ struct MmaCfg {
 // p = exp2(s - m) <= 2^TAU stay far from fp16 overflow in p * vs)
 constexpr float TAU = 4.0f;
 
-// grid (S, Hkv, n_splits), block 128
-template <int D, int BITS, int P, int NT, class IN>
+// grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store
+// (a separate instantiation, so the unrotated kernels keep their code)
+template <int D, int BITS, int P, int NT, class IN, bool ROT>
 __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB)) decode_mma_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
@@ -391,7 +392,18 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
 #pragma unroll 1
     for (int i = 0; i < NS && i < npw; i++) issue(i, __shfl_sync(0xffffffffu, btw, i));
 
-    for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm_log2;
+    if constexpr (ROT) {                              // q rotated in fp32 (canonical FWHT) as it loads, then scaled
+        for (int hd = wid; hd < G; hd += NW) {
+            float x[D / WARP];
+#pragma unroll
+            for (int i = 0; i < D / WARP; i++) x[i] = to_f32(q[qbase + hd * D + lane + WARP * i]);
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < D / WARP; i++) qsm[hd * D + lane + WARP * i] = x[i] * sm_log2;
+        }
+    } else {
+        for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm_log2;
+    }
     // kb_ref: K bias of the sequence's first page (only when one is full; a tail-only sequence uses 0)
     const uint8_t* rec0 = full > 0 ? hcache + int64_t(bt[0]) * block_stride : nullptr;
     for (int i = threadIdx.x; i < D; i += NW * WARP) {
@@ -647,6 +659,33 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
         }
     }
     __syncthreads();
+    if (ROT && n_splits == 1) {                       // one warp per head: merge, rotate back (canonical FWHT), store
+        constexpr int R = D / WARP;
+        for (int hd = wid; hd < G; hd += NW) {
+            float M = -INFINITY;
+            for (int w = 0; w <= NW; w++) M = fmaxf(M, c_m[w * G + hd]);
+            float Ls = 0.0f, x[R];
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = 0.0f;
+            if (M > -INFINITY) {
+                for (int w = 0; w <= NW; w++) {
+                    const float mw = c_m[w * G + hd];
+                    if (mw > -INFINITY) {
+                        const float f = fast_exp2(mw - M);
+                        Ls += c_l[w * G + hd] * f;
+#pragma unroll
+                        for (int i = 0; i < R; i++) x[i] += f * c_acc[(w * G + hd) * D + lane + WARP * i];
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = !ok ? NAN : Ls > 0.0f ? x[i] / Ls : 0.0f;
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < R; i++) out[qbase + hd * D + lane + WARP * i] = from_f32<IN>(x[i]);
+        }
+        return;
+    }
     for (int idx = threadIdx.x; idx < G * D; idx += NW * WARP) {
         const int hd = idx / D, d = idx % D;
         float M = -INFINITY;
@@ -720,13 +759,13 @@ bool make_page_map(const void* cache, int64_t block_stride, int64_t head_stride,
     return true;
 }
 
-template <int D, int BITS, int P, int NT, class IN>
-int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
-               const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
-               int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
-               int32_t n_seqs, cudaStream_t stream) {
+template <int D, int BITS, int P, int NT, class IN, bool ROT>
+int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
+                   const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
+                   int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
+                   int32_t n_seqs, cudaStream_t stream) {
     using C = MmaCfg<D, BITS, P, NT>;
-    auto kern = decode_mma_kernel<D, BITS, P, NT, IN>;
+    auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT>;
     CUtensorMap map;
     memset(&map, 0, sizeof(map));
     uint32_t swz_m = 0;
@@ -751,6 +790,20 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
+template <int D, int BITS, int P, int NT, class IN>
+int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
+               const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
+               int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
+               int32_t n_seqs, int rot, cudaStream_t stream) {
+    if (rot)
+        return launch_mma_rot<D, BITS, P, NT, IN, true>(G, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
+                                                        block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml,
+                                                        part_o, n_seqs, stream);
+    return launch_mma_rot<D, BITS, P, NT, IN, false>(G, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
+                                                     block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml,
+                                                     part_o, n_seqs, stream);
+}
+
 int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
     if (dtype != KUSH_F16 && dtype != KUSH_BF16) return 0;
     if ((D != 64 && D != 128 && D != 256) || (bits != 4 && bits != 8) || (P != 16 && P != 32)) return 0;
@@ -760,7 +813,7 @@ int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
 int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
                       int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                       const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
-                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, cudaStream_t stream) {
+                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, cudaStream_t stream) {
     auto go = [&](auto Dc, auto Bc, auto Pc, auto in) -> int {
         using IN = decltype(in);
         if constexpr (std::is_same_v<IN, float>) {
@@ -768,16 +821,16 @@ int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, v
         } else if constexpr (Dc.value == 256) {
             return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                    tail_idx, block_table, seq_lens, max_pages, hkv,
-                                                                   scale, n_splits, part_ml, part_o, n_seqs, stream);
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, stream);
         } else {
             if (G <= 8)
                 return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride,
                                                                        tail_k, tail_idx, block_table, seq_lens,
                                                                        max_pages, hkv, scale, n_splits, part_ml,
-                                                                       part_o, n_seqs, stream);
+                                                                       part_o, n_seqs, rot, stream);
             return launch_mma<Dc.value, Bc.value, Pc.value, 2, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                    tail_idx, block_table, seq_lens, max_pages, hkv,
-                                                                   scale, n_splits, part_ml, part_o, n_seqs, stream);
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, stream);
         }
     };
     return dispatch_fmt(D, bits, P, dtype, go);

@@ -21,7 +21,7 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
-    float sm, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o) {
+    float sm, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o, int rot) {
     using F = Fmt<D, BITS, P>;
     constexpr int NW = SIMT_NW;
     constexpr int R = D / WARP;
@@ -51,7 +51,18 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     const int32_t* bt = block_table + s * max_pages;
     const int64_t qbase = (int64_t(s) * H + h) * G * D;
 
-    for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = to_f32(q[qbase + i]) * sm;
+    for (int i = threadIdx.x; i < G * D; i += NW * WARP) qsm[i] = rot ? to_f32(q[qbase + i]) : to_f32(q[qbase + i]) * sm;
+    if (rot) {                                             // q rotated in fp32 (canonical FWHT), then scaled
+        __syncthreads();
+        for (int g = wid; g < G; g += NW) {
+            float x[R];
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = qsm[g * D + lane + WARP * i];
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < R; i++) qsm[g * D + lane + WARP * i] = x[i] * sm;
+        }
+    }
     float* qs = qs_all + wid * G * D;
     float* acc = acc_all + wid * G * D;
     float* wt = w_all + wid * G * P;
@@ -167,7 +178,8 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
             }
         }
         if (n_splits == 1) {
-            out[qbase + idx] = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
+            if (rot) qsm[idx] = L > 0.0f ? o / L : 0.0f;                // rotated back below
+            else out[qbase + idx] = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
         } else {
             const int64_t pb = ((int64_t(s) * H + h) * n_splits + z) * G + g;
             part_o[pb * D + d] = o;
@@ -175,6 +187,17 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
                 part_ml[pb * 2] = M;
                 part_ml[pb * 2 + 1] = L;
             }
+        }
+    }
+    if (rot && n_splits == 1) {                            // the output rotated back (canonical FWHT), a warp per head
+        __syncthreads();
+        for (int g = wid; g < G; g += NW) {
+            float x[R];
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = qsm[g * D + lane + WARP * i];
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < R; i++) out[qbase + g * D + lane + WARP * i] = from_f32<IN>(x[i]);
         }
     }
 }
@@ -202,11 +225,44 @@ __global__ void __launch_bounds__(256) combine_kernel(IN* __restrict__ out, cons
     out[(sh * G + g) * D + d] = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
 }
 
+// combine_kernel with the merged output rotated back (canonical FWHT) before its store: the row of D values goes
+// through shared memory to one warp
+template <int D, class IN>
+__global__ void __launch_bounds__(D) combine_rot_kernel(IN* __restrict__ out, const float* __restrict__ part_ml,
+                                                        const float* __restrict__ part_o, int n_splits, int G) {
+    __shared__ float row[D];
+    const int64_t sh = blockIdx.x / G, g = blockIdx.x % G;
+    const int d = threadIdx.x;
+    const float* ml = part_ml + (sh * n_splits * G + g) * 2;
+    const float* po = part_o + (sh * n_splits * G + g) * D + d;
+    float M = -INFINITY;
+    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ml[2 * int64_t(z) * G]);
+    float L = 0.0f, o = 0.0f;
+    for (int z = 0; z < n_splits; z++) {
+        const float mz = ml[2 * int64_t(z) * G];
+        if (mz > -INFINITY) {
+            const float f = __expf(mz - M);
+            L = fmaf(ml[2 * int64_t(z) * G + 1], f, L);
+            o = fmaf(f, po[int64_t(z) * G * D], o);
+        }
+    }
+    row[d] = L > 0.0f ? o / L : 0.0f;
+    __syncthreads();
+    if (d < WARP) {
+        float x[D / WARP];
+#pragma unroll
+        for (int i = 0; i < D / WARP; i++) x[i] = row[d + WARP * i];
+        fwht_warp<D>(x, d);
+#pragma unroll
+        for (int i = 0; i < D / WARP; i++) out[(sh * G + g) * D + d + WARP * i] = from_f32<IN>(x[i]);
+    }
+}
+
 template <int D, int BITS, int P, class IN>
 int launch_decode_simt(const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                        const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                        int64_t max_pages, int32_t hkv, int32_t G, float scale, int32_t n_splits, float* part_ml,
-                       float* part_o, int32_t n_seqs, cudaStream_t stream) {
+                       float* part_o, int32_t n_seqs, int rot, cudaStream_t stream) {
     constexpr int NW = SIMT_NW;
     const size_t smem = sizeof(float) * (size_t(G) * D + 2 * size_t(NW) * G * D + size_t(NW) * G * P + 3 * size_t(NW) * G);
     if (smem > 200 * 1024) return set_error(KUSH_ERR_UNSUPPORTED, "decode: group %d too large for head_dim %d", G, D);
@@ -216,7 +272,7 @@ int launch_decode_simt(const void* q, void* out, const void* cache, int64_t bloc
     kern<<<grid, NW * WARP, smem, stream>>>(static_cast<const IN*>(q), static_cast<IN*>(out),
                                             static_cast<const uint8_t*>(cache), block_stride, head_stride,
                                             static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens, max_pages,
-                                            hkv, G, scale, n_splits, part_ml, part_o);
+                                            hkv, G, scale, n_splits, part_ml, part_o, rot);
     return check_launch("kush_sm100_decode (cuda cores)");
 }
 
@@ -232,18 +288,41 @@ int launch_combine(void* out, const float* part_ml, const float* part_o, int32_t
 int launch_decode_simt_any(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
                            int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                            const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv,
-                           float scale, int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs,
+                           float scale, int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot,
                            cudaStream_t stream) {
     return dispatch_fmt(D, bits, P, dtype, [&](auto Dc, auto Bc, auto Pc, auto in) {
         return launch_decode_simt<Dc.value, Bc.value, Pc.value, decltype(in)>(
             q, out, cache, block_stride, head_stride, tail_k, tail_idx, block_table, seq_lens, max_pages, hkv, G,
-            scale, n_splits, part_ml, part_o, n_seqs, stream);
+            scale, n_splits, part_ml, part_o, n_seqs, rot, stream);
     });
 }
 
 }  // namespace kush
 
 using namespace kush;
+
+extern "C" int kush_sm100_combine_rotated(int32_t head_dim, int32_t dtype, int32_t group, void* out,
+                                          const float* part_ml, const float* part_o, int32_t n_splits, int32_t hkv,
+                                          int32_t n_seqs, void* stream) {
+    if (n_seqs < 0 || hkv < 1 || group < 1 || n_splits < 1)
+        return set_error(KUSH_ERR_ARG, "kush_sm100_combine_rotated: n_seqs %d hkv %d group %d n_splits %d", n_seqs, hkv,
+                         group, n_splits);
+    if (n_seqs == 0) return KUSH_OK;
+    if (!out || !part_ml || !part_o) return set_error(KUSH_ERR_ARG, "kush_sm100_combine_rotated: null pointer");
+    const int64_t blocks = int64_t(n_seqs) * hkv * group;
+    if (blocks > 0x7fffffff) return set_error(KUSH_ERR_ARG, "kush_sm100_combine_rotated: grid too large");
+    int rc = dispatch_dim(head_dim, [&](auto D) {
+        return dispatch_dtype(dtype, [&](auto in) {
+            using IN = decltype(in);
+            combine_rot_kernel<D.value, IN><<<unsigned(blocks), D.value, 0, static_cast<cudaStream_t>(stream)>>>(
+                static_cast<IN*>(out), part_ml, part_o, n_splits, group);
+            return check_launch("kush_sm100_combine_rotated");
+        });
+    });
+    if (rc == KUSH_ERR_UNSUPPORTED)
+        return set_error(rc, "kush_sm100_combine_rotated: head_dim %d / dtype %d", head_dim, dtype);
+    return rc;
+}
 
 extern "C" int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void* out, const float* part_ml,
                                   const float* part_o, int32_t n_splits, int32_t hkv, int32_t n_seqs, void* stream) {

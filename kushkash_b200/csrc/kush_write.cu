@@ -14,17 +14,15 @@
 
 namespace kush {
 
-// one warp: V token row src[0:D] -> row t of the record (per-token range: the row's final encoding)
-// (kushkash/kush/gpu.mojo:163-188 _quantize_v_row)
-template <int D, int BITS, int P, class IN>
-__device__ __forceinline__ void quantize_v_row(const IN* __restrict__ src, uint8_t* __restrict__ rec, int t, int lane) {
+// one warp: V token row x (lane l holding dims l + 32 i) -> row t of the record (per-token range: the row's final
+// encoding) (kushkash/kush/gpu.mojo:163-188 _quantize_v_row)
+template <int D, int BITS, int P>
+__device__ __forceinline__ void quantize_v_vals(const float (&x)[D / WARP], uint8_t* __restrict__ rec, int t, int lane) {
     using F = Fmt<D, BITS, P>;
     constexpr int R = D / WARP;
-    float x[R];
     float mn = INFINITY, mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < R; i++) {
-        x[i] = to_f32(src[lane + WARP * i]);
         mn = fminf(mn, x[i]);
         mx = fmaxf(mx, x[i]);
     }
@@ -43,6 +41,15 @@ __device__ __forceinline__ void quantize_v_row(const IN* __restrict__ src, uint8
         for (int i = 0; i < R / 2; i++)                    // byte j = lane + 32i holds dims j and j + D/2 = x[i + R/2]
             vc[lane + WARP * i] = pack4(qcode<4>(x[i], b, inv), qcode<4>(x[i + R / 2], b, inv));
     }
+}
+
+// one warp: V token row src[0:D] -> row t of the record
+template <int D, int BITS, int P, class IN>
+__device__ __forceinline__ void quantize_v_row(const IN* __restrict__ src, uint8_t* __restrict__ rec, int t, int lane) {
+    float x[D / WARP];
+#pragma unroll
+    for (int i = 0; i < D / WARP; i++) x[i] = to_f32(src[lane + WARP * i]);
+    quantize_v_vals<D, BITS, P>(x, rec, t, lane);
 }
 
 // K of one page by the threads of a block (kushkash/kush/gpu.mojo:121-160 _quantize_k_page): per-channel range
@@ -94,17 +101,37 @@ __global__ void __launch_bounds__(D) append_kernel(const IN* __restrict__ k_new,
                                                    int64_t k_stride, int64_t v_stride, int32_t* seq_lens, int pos_offset,
                                                    int advance, const int32_t* __restrict__ tail_idx, uint8_t* cache,
                                                    int64_t block_stride, int64_t head_stride, IN* tail_k,
-                                                   const int32_t* __restrict__ block_table, int64_t max_pages, int H) {
+                                                   const int32_t* __restrict__ block_table, int64_t max_pages, int H,
+                                                   int rot) {
     const int s = blockIdx.x, d = threadIdx.x, lane = d % WARP, w = d / WARP;
-    constexpr int NW = D / WARP;
+    constexpr int NW = D / WARP, R = D / WARP;
     const int64_t pos = int64_t(seq_lens[s]) + pos_offset;
     if (pos < 0) return;                                   // padding row
     const int slot = int(pos % P);
     const int64_t tb = int64_t(tail_idx[s]) * H * P * D;
     const int64_t blk = block_table[s * max_pages + pos / P];
-    for (int h = 0; h < H; h++) tail_k[tb + (int64_t(h) * P + slot) * D + d] = k_new[s * k_stride + h * D + d];
-    for (int h = w; h < H; h += NW)
-        quantize_v_row<D, BITS, P, IN>(v_new + s * v_stride + h * D, rec_at(cache, blk, h, block_stride, head_stride), slot, lane);
+    if (rot) {
+        // rotated rows (canonical FWHT, rounded to IN: what kush_sm100_fwht would have handed over), one warp per head
+        for (int h = w; h < H; h += NW) {
+            float x[R];
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = to_f32(k_new[s * k_stride + h * D + lane + WARP * i]);
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < R; i++) tail_k[tb + (int64_t(h) * P + slot) * D + lane + WARP * i] = from_f32<IN>(x[i]);
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = to_f32(v_new[s * v_stride + h * D + lane + WARP * i]);
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = to_f32(from_f32<IN>(x[i]));
+            quantize_v_vals<D, BITS, P>(x, rec_at(cache, blk, h, block_stride, head_stride), slot, lane);
+        }
+    } else {
+        for (int h = 0; h < H; h++) tail_k[tb + (int64_t(h) * P + slot) * D + d] = k_new[s * k_stride + h * D + d];
+        for (int h = w; h < H; h += NW)
+            quantize_v_row<D, BITS, P, IN>(v_new + s * v_stride + h * D, rec_at(cache, blk, h, block_stride, head_stride),
+                                           slot, lane);
+    }
     __syncthreads();                                       // tail rows visible to the page quantizer; seq_lens read
     if (slot == P - 1) {
         for (int h = 0; h < H; h++) {
@@ -1043,11 +1070,11 @@ template <int D, int BITS, int P, class IN>
 int launch_append(const void* k_new, const void* v_new, int64_t k_stride, int64_t v_stride, int32_t* seq_lens,
                   int32_t pos_offset, int32_t advance, const int32_t* tail_idx, void* cache, int64_t block_stride,
                   int64_t head_stride, void* tail_k, const int32_t* block_table, int64_t max_pages, int32_t hkv,
-                  int32_t n_seqs, cudaStream_t stream) {
+                  int32_t n_seqs, int rot, cudaStream_t stream) {
     append_kernel<D, BITS, P, IN><<<n_seqs, D, 0, stream>>>(
         static_cast<const IN*>(k_new), static_cast<const IN*>(v_new), k_stride, v_stride, seq_lens, pos_offset, advance,
         tail_idx, static_cast<uint8_t*>(cache), block_stride, head_stride, static_cast<IN*>(tail_k), block_table,
-        max_pages, hkv);
+        max_pages, hkv, rot);
     return check_launch("kush_sm100_append");
 }
 
@@ -1163,24 +1190,45 @@ int write_error_flag(int clear) {
 
 using namespace kush;
 
+static int append_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void* k_new,
+                      const void* v_new, int64_t k_stride, int64_t v_stride, int32_t* seq_lens, int32_t pos_offset,
+                      int32_t advance, const int32_t* tail_idx, void* cache, int64_t block_stride, int64_t head_stride,
+                      void* tail_k, const int32_t* block_table, int64_t max_pages, int32_t hkv, int32_t n_seqs, int rot,
+                      void* stream, const char* name) {
+    if (n_seqs < 0 || hkv < 1) return set_error(KUSH_ERR_ARG, "%s: n_seqs %d, hkv %d", name, n_seqs, hkv);
+    if (n_seqs == 0) return KUSH_OK;
+    if (!k_new || !v_new || !seq_lens || !tail_idx || !cache || !tail_k || !block_table)
+        return set_error(KUSH_ERR_ARG, "%s: null pointer", name);
+    int rc = dispatch_fmt(head_dim, bits, page, dtype, [&](auto D, auto B, auto P, auto in) {
+        return launch_append<D.value, B.value, P.value, decltype(in)>(
+            k_new, v_new, k_stride, v_stride, seq_lens, pos_offset, advance, tail_idx, cache, block_stride, head_stride,
+            tail_k, block_table, max_pages, hkv, n_seqs, rot, static_cast<cudaStream_t>(stream));
+    });
+    if (rc == KUSH_ERR_UNSUPPORTED)
+        return set_error(rc, "%s: unsupported head_dim %d / bits %d / page %d / dtype %d", name, head_dim, bits, page,
+                         dtype);
+    return rc;
+}
+
 extern "C" int kush_sm100_append(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void* k_new,
                                  const void* v_new, int64_t k_stride, int64_t v_stride, int32_t* seq_lens,
                                  int32_t pos_offset, int32_t advance, const int32_t* tail_idx, void* cache,
                                  int64_t block_stride, int64_t head_stride, void* tail_k, const int32_t* block_table,
                                  int64_t max_pages, int32_t hkv, int32_t n_seqs, void* stream) {
-    if (n_seqs < 0 || hkv < 1) return set_error(KUSH_ERR_ARG, "kush_sm100_append: n_seqs %d, hkv %d", n_seqs, hkv);
-    if (n_seqs == 0) return KUSH_OK;
-    if (!k_new || !v_new || !seq_lens || !tail_idx || !cache || !tail_k || !block_table)
-        return set_error(KUSH_ERR_ARG, "kush_sm100_append: null pointer");
-    int rc = dispatch_fmt(head_dim, bits, page, dtype, [&](auto D, auto B, auto P, auto in) {
-        return launch_append<D.value, B.value, P.value, decltype(in)>(
-            k_new, v_new, k_stride, v_stride, seq_lens, pos_offset, advance, tail_idx, cache, block_stride, head_stride,
-            tail_k, block_table, max_pages, hkv, n_seqs, static_cast<cudaStream_t>(stream));
-    });
-    if (rc == KUSH_ERR_UNSUPPORTED)
-        return set_error(rc, "kush_sm100_append: unsupported head_dim %d / bits %d / page %d / dtype %d", head_dim, bits,
-                         page, dtype);
-    return rc;
+    return append_any(head_dim, bits, page, dtype, k_new, v_new, k_stride, v_stride, seq_lens, pos_offset, advance,
+                      tail_idx, cache, block_stride, head_stride, tail_k, block_table, max_pages, hkv, n_seqs, 0, stream,
+                      "kush_sm100_append");
+}
+
+extern "C" int kush_sm100_append_rotated(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype,
+                                         const void* k_new, const void* v_new, int64_t k_stride, int64_t v_stride,
+                                         int32_t* seq_lens, int32_t pos_offset, int32_t advance,
+                                         const int32_t* tail_idx, void* cache, int64_t block_stride,
+                                         int64_t head_stride, void* tail_k, const int32_t* block_table,
+                                         int64_t max_pages, int32_t hkv, int32_t n_seqs, void* stream) {
+    return append_any(head_dim, bits, page, dtype, k_new, v_new, k_stride, v_stride, seq_lens, pos_offset, advance,
+                      tail_idx, cache, block_stride, head_stride, tail_k, block_table, max_pages, hkv, n_seqs, 1, stream,
+                      "kush_sm100_append_rotated");
 }
 
 extern "C" int kush_sm100_write(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void* k_new,

@@ -338,6 +338,64 @@ def test_ragged_mixed_batches(bits, D, G, P):
             step(reqs, qls)
 
 
+# ---------------------------------------------------------------- rotation fused into the decode step
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("D,bits,P", [(128, 4, 16), (64, 8, 32), (256, 4, 32), (128, 8, 16)])
+def test_append_rotated_equals_fwht_then_append(D, bits, P, dtype):
+    """append(rotate=True) stores exactly what fwht() then append() store: pages (including the K pages the
+    append completes from the tail) and tail rows, over 2 P + 3 steps."""
+    H, B = 2, 3
+    g = torch.Generator().manual_seed(D + bits + P)
+    steps = 2 * P + 3
+    pages = -(-steps // P)
+    bt = torch.randperm(B * pages, generator=g).to(torch.int32).view(B, pages)
+    ops = gpu_ops(D, bits, 1, dtype, P)
+    st_a = make_state(B, H, D, bits, P, bt, B * pages, "cuda", dtype)
+    st_b = make_state(B, H, D, bits, P, bt, B * pages, "cuda", dtype)
+    off = torch.randn(H, D, generator=g) * 3
+    for _ in range(steps):
+        k = (torch.randn(B, H, D, generator=g) + off).to("cuda", dtype)
+        v = torch.randn(B, H, D, generator=g).to("cuda", dtype)
+        ops.append(ops.fwht(k), ops.fwht(v), st_a.seq_lens, st_a.tail_idx, st_a.pool, st_a.block_table, st_a.tail_k,
+                   pos_offset=0, advance=True)
+        ops.append(k, v, st_b.seq_lens, st_b.tail_idx, st_b.pool, st_b.block_table, st_b.tail_k, pos_offset=0,
+                   advance=True, rotate=True)
+    assert torch.equal(st_a.pool, st_b.pool)
+    assert torch.equal(st_a.tail_k, st_b.tail_k) and torch.equal(st_a.seq_lens, st_b.seq_lens)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("n_splits", [1, 3])
+@pytest.mark.parametrize("D,bits,G,P,n", [(128, 4, 4, 16, 150), (64, 8, 3, 32, 77), (256, 4, 2, 32, 100)])
+def test_decode_rotated(D, bits, G, P, n, n_splits, dtype):
+    """decode(rotate=True) over a rotated cache equals the oracle's fwht(q) -> decode -> fwht(out) (fp32) within the
+    decode tolerance, as the unfused GPU sequence does (bf16 / fp16: tensor-core kernel; fp32: CUDA-core kernel)."""
+    B, H = 2, 2
+    c = decode_inputs(D, bits, G, P, B, H, n)
+    ro, ops = OracleOps(D, bits, G, P), gpu_ops(D, bits, G, dtype, P)
+    K, V, q = exact(c["K"], dtype), exact(c["V"], dtype), exact(c["q"], dtype)
+    Kr, Vr = exact(ro.fwht(K.contiguous()), dtype), exact(ro.fwht(V.contiguous()), dtype)   # the rotated cache
+    ref = make_state(B, H, D, bits, P, c["block_table"], c["n_blocks"])
+    fill(ro, ref, Kr, Vr, n, torch.float32, "cpu")
+    want = torch.empty(B, H * G, D)
+    ro.decode(ro.fwht(q.contiguous()), want, ref.pool, ref.block_table, ref.seq_lens, ref.tail_idx, ref.tail_k,
+              D ** -0.5)
+    want = ro.fwht(want)
+    st = make_state(B, H, D, bits, P, c["block_table"], c["n_blocks"], "cuda", dtype)
+    fill(ops, st, Kr, Vr, n, dtype, "cuda")
+    assert torch.equal(st.pool.cpu(), ref.pool)
+    work = torch.empty(ops.work_size(B, H, n_splits), device="cuda")
+    qd = q.to("cuda", dtype).contiguous()
+    out = torch.empty(B, H * G, D, dtype=dtype, device="cuda")
+    ops.decode(qd, out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5, n_splits, work,
+               rotate=True)
+    assert_close(out, want, dtype, f"rotated decode D{D} int{bits} P{P} splits {n_splits}")
+    unfused = torch.empty_like(out)
+    ops.decode(ops.fwht(qd), unfused, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5,
+               n_splits, work)
+    assert_close(ops.fwht(unfused), want, dtype, "unfused")
+
+
 # ---------------------------------------------------------------- KushCache end to end
 @pytest.mark.parametrize("rot", [False, True])
 @pytest.mark.parametrize("P", [16, 32])
