@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     using L = Lay<D, BITS>;
     using C = MmaCfg<D, BITS, P, NT>;
     constexpr int NW = MMA_NW, NS = C::NS, KT = L::KT, MT = L::MT, MTT = P / 16;
+    pdl_wait();                                                         // previous kernel on the stream done
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // [NW][NS]
     const uint32_t smem0 = smem_u32(smem);
@@ -782,11 +783,10 @@ int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t b
         attr_set |= 1ull << (dev & 63);
     }
     dim3 grid(n_seqs, hkv, n_splits);
-    kern<<<grid, MMA_NW * WARP, C::SMEM, stream>>>(static_cast<const IN*>(q), static_cast<IN*>(out),
-                                                   static_cast<const uint8_t*>(cache), block_stride, head_stride,
-                                                   static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens,
-                                                   max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml,
-                                                   part_o, map, tma ? 1 : 0, swz_m, rows_per_head, box_rows);
+    launch_pdl(kern, grid, dim3(MMA_NW * WARP), C::SMEM, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
+               static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
+               block_table, seq_lens, max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml, part_o, map,
+               tma ? 1 : 0, swz_m, rows_per_head, box_rows);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 

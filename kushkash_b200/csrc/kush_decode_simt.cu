@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     float sm, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o, int rot) {
     using F = Fmt<D, BITS, P>;
     constexpr int NW = SIMT_NW;
+    pdl_wait();                                            // previous kernel on the stream done
     constexpr int R = D / WARP;
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
@@ -207,6 +208,7 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
 template <class IN>
 __global__ void __launch_bounds__(256) combine_kernel(IN* __restrict__ out, const float* __restrict__ part_ml,
                                                       const float* __restrict__ part_o, int n_splits, int G, int D) {
+    pdl_wait();                                            // previous kernel on the stream done
     const int64_t sh = blockIdx.x / G, g = blockIdx.x % G;
     const int d = threadIdx.x;
     const float* ml = part_ml + (sh * n_splits * G + g) * 2;     // split z at ml[2 z G]
@@ -231,6 +233,8 @@ template <int D, class IN>
 __global__ void __launch_bounds__(D) combine_rot_kernel(IN* __restrict__ out, const float* __restrict__ part_ml,
                                                         const float* __restrict__ part_o, int n_splits, int G) {
     __shared__ float row[D];
+    pdl_wait();                                            // previous kernel on the stream done
+
     const int64_t sh = blockIdx.x / G, g = blockIdx.x % G;
     const int d = threadIdx.x;
     const float* ml = part_ml + (sh * n_splits * G + g) * 2;
@@ -269,10 +273,9 @@ int launch_decode_simt(const void* q, void* out, const void* cache, int64_t bloc
     auto kern = decode_simt_kernel<D, BITS, P, IN>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     dim3 grid(n_seqs, hkv, n_splits);
-    kern<<<grid, NW * WARP, smem, stream>>>(static_cast<const IN*>(q), static_cast<IN*>(out),
-                                            static_cast<const uint8_t*>(cache), block_stride, head_stride,
-                                            static_cast<const IN*>(tail_k), tail_idx, block_table, seq_lens, max_pages,
-                                            hkv, G, scale, n_splits, part_ml, part_o, rot);
+    launch_pdl(kern, grid, dim3(NW * WARP), smem, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
+               static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
+               block_table, seq_lens, max_pages, hkv, G, scale, n_splits, part_ml, part_o, rot);
     return check_launch("kush_sm100_decode (cuda cores)");
 }
 
@@ -281,7 +284,8 @@ int launch_combine(void* out, const float* part_ml, const float* part_o, int32_t
                    int32_t D, int32_t n_seqs, cudaStream_t stream) {
     const int64_t blocks = int64_t(n_seqs) * hkv * G;
     if (blocks > 0x7fffffff) return set_error(KUSH_ERR_ARG, "kush_sm100_combine: grid too large");
-    combine_kernel<IN><<<unsigned(blocks), D, 0, stream>>>(static_cast<IN*>(out), part_ml, part_o, n_splits, G, D);
+    launch_pdl(combine_kernel<IN>, dim3(unsigned(blocks)), dim3(D), 0, stream, static_cast<IN*>(out), part_ml, part_o,
+               n_splits, G, D);
     return check_launch("kush_sm100_combine");
 }
 
@@ -314,8 +318,8 @@ extern "C" int kush_sm100_combine_rotated(int32_t head_dim, int32_t dtype, int32
     int rc = dispatch_dim(head_dim, [&](auto D) {
         return dispatch_dtype(dtype, [&](auto in) {
             using IN = decltype(in);
-            combine_rot_kernel<D.value, IN><<<unsigned(blocks), D.value, 0, static_cast<cudaStream_t>(stream)>>>(
-                static_cast<IN*>(out), part_ml, part_o, n_splits, group);
+            launch_pdl(combine_rot_kernel<D.value, IN>, dim3(unsigned(blocks)), dim3(D.value), 0,
+                       static_cast<cudaStream_t>(stream), static_cast<IN*>(out), part_ml, part_o, n_splits, group);
             return check_launch("kush_sm100_combine_rotated");
         });
     });

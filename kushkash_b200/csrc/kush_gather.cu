@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(IN* const* __restri
                                                              const float* __restrict__ part_o, int n_splits, int G,
                                                              int D, int H, uint32_t* const* __restrict__ flags,
                                                              uint32_t* __restrict__ ctr) {
+    pdl_wait();                                       // previous kernel on the stream done
     const int64_t sh = blockIdx.x / G, g = blockIdx.x % G;
     const int64_t s = sh / H, h = sh % H;
     const int d = threadIdx.x;
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(IN* const* __restri
 // rank's own count, written by its combine_gather earlier in the stream)
 __global__ void __launch_bounds__(32) gather_wait_kernel(const uint32_t* __restrict__ flags, int world,
                                                          const uint32_t* __restrict__ ctr) {
+    pdl_wait();                                       // previous kernel on the stream done
     const int lane = threadIdx.x;
     const uint32_t seq = *reinterpret_cast<const volatile uint32_t*>(ctr + 1);
     bool ok = true;
@@ -166,9 +168,9 @@ extern "C" int kush_sm100_combine_gather(int32_t head_dim, int32_t dtype, int32_
     const int hq_total = hkv * world * group;
     int rc = dispatch_dtype(dtype, [&](auto in) {
         using IN = decltype(in);
-        combine_gather_kernel<IN><<<unsigned(blocks), head_dim, 0, static_cast<cudaStream_t>(stream)>>>(
-            reinterpret_cast<IN* const*>(outs), rank, world, hq_total, part_ml, part_o, n_splits, group, head_dim,
-            hkv, flags, ctr);
+        launch_pdl(combine_gather_kernel<IN>, dim3(unsigned(blocks)), dim3(head_dim), 0,
+                   static_cast<cudaStream_t>(stream), reinterpret_cast<IN* const*>(outs), rank, world, hq_total,
+                   part_ml, part_o, n_splits, group, head_dim, hkv, flags, ctr);
         return check_launch("kush_sm100_combine_gather");
     });
     if (rc == KUSH_ERR_UNSUPPORTED) return set_error(rc, "kush_sm100_combine_gather: dtype %d", dtype);
@@ -178,6 +180,6 @@ extern "C" int kush_sm100_combine_gather(int32_t head_dim, int32_t dtype, int32_
 extern "C" int kush_sm100_gather_wait(const uint32_t* flags, int32_t world, const uint32_t* ctr, void* stream) {
     if (world < 1 || world > 32 || !flags || !ctr)
         return set_error(KUSH_ERR_ARG, "kush_sm100_gather_wait: world %d or null pointer", world);
-    gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, ctr);
+    launch_pdl(gather_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), flags, world, ctr);
     return check_launch("kush_sm100_gather_wait");
 }

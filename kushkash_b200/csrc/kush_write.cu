@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(D) append_kernel(const IN* __restrict__ k_new,
                                                    int64_t block_stride, int64_t head_stride, IN* tail_k,
                                                    const int32_t* __restrict__ block_table, int64_t max_pages, int H,
                                                    int rot) {
+    pdl_wait();                                       // previous kernel on the stream done
     const int s = blockIdx.x, d = threadIdx.x, lane = d % WARP, w = d / WARP;
     constexpr int NW = D / WARP, R = D / WARP;
     const int64_t pos = int64_t(seq_lens[s]) + pos_offset;
@@ -1071,10 +1072,10 @@ int launch_append(const void* k_new, const void* v_new, int64_t k_stride, int64_
                   int32_t pos_offset, int32_t advance, const int32_t* tail_idx, void* cache, int64_t block_stride,
                   int64_t head_stride, void* tail_k, const int32_t* block_table, int64_t max_pages, int32_t hkv,
                   int32_t n_seqs, int rot, cudaStream_t stream) {
-    append_kernel<D, BITS, P, IN><<<n_seqs, D, 0, stream>>>(
-        static_cast<const IN*>(k_new), static_cast<const IN*>(v_new), k_stride, v_stride, seq_lens, pos_offset, advance,
-        tail_idx, static_cast<uint8_t*>(cache), block_stride, head_stride, static_cast<IN*>(tail_k), block_table,
-        max_pages, hkv, rot);
+    launch_pdl(append_kernel<D, BITS, P, IN>, dim3(n_seqs), dim3(D), 0, stream, static_cast<const IN*>(k_new),
+               static_cast<const IN*>(v_new), k_stride, v_stride, seq_lens, pos_offset, advance, tail_idx,
+               static_cast<uint8_t*>(cache), block_stride, head_stride, static_cast<IN*>(tail_k), block_table,
+               max_pages, hkv, rot);
     return check_launch("kush_sm100_append");
 }
 
