@@ -427,6 +427,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     ap.add_argument("--cpu-seqs", type=int, default=32, help="sequences in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch-order", choices=["longest", "natural"], default="longest",
+                    help="ragged workloads (configs 2, 5): decode CTAs take the sequences longest first (an order "
+                         "computed once per step) or in their natural order")
     ap.add_argument("--rotate", choices=["none", "fused", "unfused"], default="none",
                     help="config 3 with the Walsh-Hadamard rotation of kushkash's 4-bit default: inside the append and "
                          "decode kernels (fused) or as fwht launches around them (unfused); BASELINE runs without")
@@ -756,7 +759,7 @@ class RaggedEngine:
     of every sequence) for the write roofline."""
 
     def __init__(self, cfg: dict, lens: list[int], n_prompts: int, device: torch.device, seed: int,
-                 extra_tokens: int, keep_fill: bool):
+                 extra_tokens: int, keep_fill: bool, launch_order: str = "natural"):
         from kushkash_b200 import Ops
         self.dev, self.L, self.lens, self.PR = device, cfg["layers"], lens, n_prompts
         self.D, self.HKV, self.HQ, self.bits, self.P = 128, cfg["hkv"], cfg["hq"], cfg["bits"], cfg["P"]
@@ -803,6 +806,12 @@ class RaggedEngine:
         self.v_new = torch.randn(L, max(S, 1), H, D, generator=dgen, device=device).to(torch.bfloat16)
         self.q = torch.randn(L, max(S, 1), self.HQ, D, generator=dgen, device=device).to(torch.bfloat16)
         self.out = torch.empty_like(self.q)
+        # longest-first decode launch order for ragged lengths over several waves of CTAs (computed once per step: the
+        # layers share lengths); measured: config 5 (16k CTAs) step -4%, config 2 (512 CTAs, one wave) no gain
+        self.order = None
+        waves = S * H * self.ns / (4 * torch.cuda.get_device_properties(device).multi_processor_count)
+        if launch_order == "longest" and S > 1 and min(lens) != max(lens) and waves > 2:
+            self.order = torch.empty(S, dtype=torch.int32, device=device)
 
     def _jobs(self, seqs: list[int]):
         """Ragged write arguments for the whole contexts of `seqs`: query_start_loc over all S, job (seq, page)."""
@@ -856,10 +865,12 @@ class RaggedEngine:
 
     def decode(self, layer: int) -> None:
         self.ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.bt_dec, self.sl_dec[layer], self.ti_dec,
-                        self.tail_dec[layer], self.scale, self.ns, self.work)
+                        self.tail_dec[layer], self.scale, self.ns, self.work, order=self.order)
 
     def step(self) -> None:
         """One step of every layer: the prompts' bulk prefill-quantize (config 5), append + decode of every sequence."""
+        if self.order is not None:
+            self.ops.longest_first(self.sl_dec[0], out=self.order)
         for layer in range(self.L):
             if self.PR:
                 self.prefill(layer)
@@ -896,7 +907,8 @@ class RaggedEngine:
         return self.S * self.HKV * (4 * self.D + self.DC + 4 + 2 * self.D)
 
     def launches_per_step(self) -> int:
-        return self.L * ((1 if self.PR else 0) + ((2 + (1 if self.ns > 1 else 0)) if self.S else 0))
+        return (self.L * ((1 if self.PR else 0) + ((2 + (1 if self.ns > 1 else 0)) if self.S else 0))
+                + (1 if self.order is not None else 0))
 
 
 def time_graph(gr, dev, reps: int = 3) -> float:
@@ -1000,7 +1012,7 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
     lens = [lens_all[i] for i in mine]
     n_pr = cfg["prompts"] // world
     eng = RaggedEngine(cfg, lens, n_pr, dev, seed=cfg["seed"] * 100 + rank, extra_tokens=a.warmup + 2 * a.steps + 8,
-                       keep_fill=n_pr == 0)
+                       keep_fill=n_pr == 0, launch_order=a.launch_order)
     kern = {}
     if n_pr == 0:                                   # write roofline: layer 0's whole contexts again
         wgraph = capture(eng.rewrite, dev)
@@ -1096,6 +1108,7 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
                        "cached_tokens": sum(lens_all), "layers_timed": eng.L, "page": cfg["P"], "bits": cfg["bits"],
                        "q_heads": cfg["hq"], "kv_heads": cfg["hkv"], "head_dim": 128,
                        "parallelism": f"requests partitioned over {world} GPU(s) by tokens, no collective in the step",
+                       "launch_order": "longest first" if eng.order is not None else "natural",
                        "l2": ("inputs larger than L2 (GBs of records per layer-step, no flush needed)" if which == "mix"
                               else "inputs smaller than L2: the graph replays re-read L2-resident records (launch- "
                                    "and latency-bound sizes, as the config intends)")},

@@ -128,6 +128,26 @@ int kush_sm100_decode_rotated(int32_t head_dim, int32_t bits, int32_t page, int3
 int kush_sm100_combine_rotated(int32_t head_dim, int32_t dtype, int32_t group, void *out, const float *part_ml,
                                const float *part_o, int32_t n_splits, int32_t hkv, int32_t n_seqs, void *stream);
 
+/* ---- Launch order of the decode.  CTA x of a decode normally works on sequence x; with ragged lengths and many waves
+ * of CTAs, a long sequence that starts in the last wave sets the end of the launch.  No counterpart in the
+ * reference. */
+
+/* order[0..n_seqs) = the sequences ranked by full pages (seq_lens / page), most first; ties in any order, pages
+ * above 4095 share the top rank.  One CTA; compute it once per step (the layers share seq_lens). */
+int kush_sm100_order_longest_first(const int32_t *seq_lens, int32_t n_seqs, int32_t page, int32_t *order,
+                                   void *stream);
+
+#define KUSH_DECODE_ROTATE 1 /* kush_sm100_decode_ex flag: as kush_sm100_decode_rotated */
+
+/* kush_sm100_decode with options: flags (KUSH_DECODE_ROTATE) and, if order is not NULL, CTA x working on sequence
+ * order[x] (a permutation of 0..n_seqs-1, e.g. from kush_sm100_order_longest_first).  The outputs do not depend on
+ * the order; the rotated tensor-core decode runs in the natural order. */
+int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group, const void *q,
+                         void *out, const void *cache, int64_t block_stride, int64_t head_stride, const void *tail_k,
+                         const int32_t *tail_idx, const int32_t *block_table, const int32_t *seq_lens,
+                         int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o,
+                         int32_t n_seqs, int32_t flags, const int32_t *order, void *stream);
+
 /* Which decode kernel a configuration takes: 1 = tensor-core kernel (mma), 0 = CUDA-core kernel,
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);

@@ -38,6 +38,9 @@ SIGNATURES = {
     "kush_sm100_decode_rotated": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,
                                   _f32, _i32, _p, _p, _i32, _p],
     "kush_sm100_combine_rotated": [_i32, _i32, _i32, _p, _p, _p, _i32, _i32, _i32, _p],
+    "kush_sm100_decode_ex": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32,
+                             _i32, _p, _p, _i32, _i32, _p, _p],
+    "kush_sm100_order_longest_first": [_p, _i32, _i32, _p, _p],
     "kush_sm100_decode_noalloc": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,
                                   _f32, _i32, _i32, _p],
     "kush_sm100_decode_tensor_cores": [_i32, _i32, _i32, _i32, _i32],
@@ -187,6 +190,17 @@ class Kernel:
                        seq_lens, max_pages, hkv, scale, n_splits, part_ml or None, part_o or None, grid[0],
                        raw_stream(self.device))
 
+    # the decode's arguments, then flags and the launch order
+    def _decode_ex(self, grid, q, out, cache, bs, hs, tail_k, tail_idx, bt, seq_lens, max_pages, hkv, scale, n_splits,
+                   part_ml, part_o, flags, order):
+        c = self.cfg
+        return self.fn(c.head_dim, c.bits, c.page, c.dtype_code, c.group, q, out, cache, bs, hs, tail_k, tail_idx, bt,
+                       seq_lens, max_pages, hkv, scale, n_splits, part_ml or None, part_o or None, grid[0], flags,
+                       order or None, raw_stream(self.device))
+
+    def _order_longest_first(self, grid, seq_lens, n_seqs, order):
+        return self.fn(seq_lens, n_seqs, self.cfg.page, order, raw_stream(self.device))
+
     # gpu.mojo:469-470 argument order
     def _combine(self, grid, out, part_ml, part_o, n_splits, hkv):
         c = self.cfg
@@ -207,7 +221,8 @@ class Kernel:
                        raw_stream(self.device))
 
 
-NAMES = ("append", "write", "decode", "combine", "fwht", "unpack", "append_rotated", "decode_rotated", "combine_rotated")
+NAMES = ("append", "write", "decode", "combine", "fwht", "unpack", "append_rotated", "decode_rotated", "combine_rotated",
+         "decode_ex", "order_longest_first")
 
 
 @lru_cache(None)

@@ -170,17 +170,19 @@ class Ops:
 
     def decode(self, q: torch.Tensor, out: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor,
-               scale: float, n_splits: int = 1, work: torch.Tensor | None = None, *, rotate: bool = False) -> None:
+               scale: float, n_splits: int = 1, work: torch.Tensor | None = None, *, rotate: bool = False,
+               order: torch.Tensor | None = None) -> None:
         """out[s] = attention of q[s] ([Hq, D]) over the seq_lens[s] cached tokens of sequence s
         (kushkash/_ops.py:191-213).  n_splits > 1 needs `work` (fp32, >= S*Hkv*n_splits*G*(D+2) elements).
         rotate=True (an extension, for a cache written with rotation): q is rotated inside the kernel and the output
-        rotated back before its store, in place of fwht(q) before and fwht(out) after."""
+        rotated back before its store, in place of fwht(q) before and fwht(out) after.  order (an extension): an int32
+        permutation of the S sequences, CTA x decoding sequence order[x] (longest_first()); same outputs."""
         S, H = q.shape[0], tail_k.shape[1]
         part_ml = part_o = 0
         if n_splits > 1:
             part_ml, part_o = self._parts(S, H, n_splits, work)
         self._decode(q, out.data_ptr(), cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, part_ml,
-                     part_o, rotate)
+                     part_o, rotate, order)
         if n_splits > 1:
             self.k["combine_rotated" if rotate else "combine"]((S, H, 1), 256, out.data_ptr(), part_ml, part_o,
                                                                n_splits, H)
@@ -207,12 +209,30 @@ class Ops:
         return work.data_ptr(), work.data_ptr() + nml * 4
 
     def _decode(self, q, out_ptr: int, cache, block_table, seq_lens, tail_idx, tail_k, scale: float, n_splits: int,
-                part_ml: int, part_o: int, rotate: bool = False) -> None:
+                part_ml: int, part_o: int, rotate: bool = False, order: torch.Tensor | None = None) -> None:
         S, H = q.shape[0], tail_k.shape[1]
         bs, hs = _byte_strides(cache)
-        self.k["decode_rotated" if rotate else "decode"]((S, H, n_splits), 32 * self.cfg.warps, q.data_ptr(), out_ptr, cache.data_ptr(), bs, hs,
-                         tail_k.data_ptr(), tail_idx.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
-                         block_table.stride(0), H, float(scale), n_splits, part_ml, part_o)
+        args = (q.data_ptr(), out_ptr, cache.data_ptr(), bs, hs, tail_k.data_ptr(), tail_idx.data_ptr(),
+                block_table.data_ptr(), seq_lens.data_ptr(), block_table.stride(0), H, float(scale), n_splits, part_ml,
+                part_o)
+        if order is None:
+            self.k["decode_rotated" if rotate else "decode"]((S, H, n_splits), 32 * self.cfg.warps, *args)
+            return
+        if order.dtype != torch.int32 or order.numel() != S or not order.is_contiguous():
+            raise ValueError("decode: order must be a contiguous int32 permutation of the sequences")
+        self.k["decode_ex"]((S, H, n_splits), 32 * self.cfg.warps, *args, 1 if rotate else 0, order.data_ptr())
+
+    def longest_first(self, seq_lens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """A launch order for decode(order=): the sequences by full pages, most first (one small kernel; compute it
+        once per step, as the layers share seq_lens).  No counterpart in the reference."""
+        S = seq_lens.numel()
+        if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
+            raise ValueError("longest_first: seq_lens must be contiguous int32")
+        out = torch.empty(S, dtype=torch.int32, device=seq_lens.device) if out is None else out
+        if out.dtype != torch.int32 or out.numel() != S or not out.is_contiguous():
+            raise ValueError("longest_first: out must be a contiguous int32 tensor of n_seqs entries")
+        self.k["order_longest_first"]((1, 1, 1), 1024, seq_lens.data_ptr(), S, out.data_ptr())
+        return out
 
 
 # ---------------------------------------------------------------- format helpers (pure PyTorch, for tests / callers)

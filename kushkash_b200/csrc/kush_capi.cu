@@ -27,12 +27,13 @@ int launch_decode_simt_any(int D, int bits, int P, int dtype, int G, const void*
                            int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                            const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv,
                            float scale, int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot,
-                           cudaStream_t stream);
+                           const int32_t* order, cudaStream_t stream);
 int decode_mma_supported(int D, int bits, int P, int dtype, int G);
 int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
                       int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                       const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
-                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, cudaStream_t stream);
+                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, const int32_t* order,
+                      cudaStream_t stream);
 
 }  // namespace kush
 
@@ -60,7 +61,8 @@ static int decode_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
                                  const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                                  const void* tail_k, const int32_t* tail_idx, const int32_t* block_table,
                                  const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
-                                 float* part_ml, float* part_o, int32_t n_seqs, int rot, void* stream) {
+                                 float* part_ml, float* part_o, int32_t n_seqs, int rot, const int32_t* order,
+                                 void* stream) {
     if (n_seqs < 0 || hkv < 1 || group < 1 || n_splits < 1)
         return set_error(KUSH_ERR_ARG, "kush_sm100_decode: n_seqs %d hkv %d group %d n_splits %d", n_seqs, hkv, group,
                          n_splits);
@@ -79,11 +81,11 @@ static int decode_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
     if (decode_mma_supported(head_dim, bits, page, dtype, group))
         return launch_decode_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
                                  tail_idx, block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o,
-                                 n_seqs, rot, st);
+                                 n_seqs, rot, order, st);
     g_err[0] = 0;
     int rc = launch_decode_simt_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
                                     tail_idx, block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o,
-                                    n_seqs, rot, st);
+                                    n_seqs, rot, order, st);
     if (rc == KUSH_ERR_UNSUPPORTED && g_err[0] == 0)
         return set_error(rc, "kush_sm100_decode: unsupported head_dim %d / bits %d / page %d / dtype %d", head_dim, bits,
                          page, dtype);
@@ -96,7 +98,8 @@ extern "C" int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, i
                                  const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
                                  float* part_ml, float* part_o, int32_t n_seqs, void* stream) {
     return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
-                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs, 0, stream);
+                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs, 0, nullptr,
+                      stream);
 }
 
 extern "C" int kush_sm100_decode_rotated(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
@@ -106,5 +109,18 @@ extern "C" int kush_sm100_decode_rotated(int32_t head_dim, int32_t bits, int32_t
                                          int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
                                          int32_t n_seqs, void* stream) {
     return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
-                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs, 1, stream);
+                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs, 1, nullptr,
+                      stream);
+}
+
+extern "C" int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+                                    const void* q, void* out, const void* cache, int64_t block_stride,
+                                    int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
+                                    const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages,
+                                    int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
+                                    int32_t n_seqs, int32_t flags, const int32_t* order, void* stream) {
+    if (flags & ~KUSH_DECODE_ROTATE) return set_error(KUSH_ERR_ARG, "kush_sm100_decode_ex: unknown flags %d", flags);
+    return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
+                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs,
+                      (flags & KUSH_DECODE_ROTATE) ? 1 : 0, order, stream);
 }

@@ -312,15 +312,16 @@ struct MmaCfg {
 // p = exp2(s - m) <= 2^TAU stay far from fp16 overflow in p * vs)
 constexpr float TAU = 4.0f;
 
-// grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store
-// (a separate instantiation, so the unrotated kernels keep their code)
-template <int D, int BITS, int P, int NT, class IN, bool ROT>
+// grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store;
+// ORD: CTA x works on sequence order[x] (separate instantiations, so the plain kernels keep their code)
+template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD>
 __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB)) decode_mma_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
     float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o,
-    const __grid_constant__ CUtensorMap tmap, int use_tma, uint32_t swz_m, int32_t rows_per_head, int32_t box_rows) {
+    const __grid_constant__ CUtensorMap tmap, int use_tma, uint32_t swz_m, int32_t rows_per_head, int32_t box_rows,
+    const int32_t* __restrict__ order) {
     using F = Fmt<D, BITS, P>;
     using L = Lay<D, BITS>;
     using C = MmaCfg<D, BITS, P, NT>;
@@ -333,7 +334,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     float* qsm = reinterpret_cast<float*>(ring + C::RING);              // [G][D] q * scale * log2e
     float* kbr = qsm + G * D;                                           // [D] kb_ref
     __half* kb16 = reinterpret_cast<__half*>(kbr + D);                  // [D] kb_ref as fp16 (read in K pair order)
-    const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
+    const int s = ORD ? order[blockIdx.x] : blockIdx.x, h = blockIdx.y, z = blockIdx.z;     // launch order
     const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP, g = lane >> 2, tid = lane & 3;
     const int64_t n = seq_lens[s];
     const int tail_n = int(n % P);
@@ -760,13 +761,13 @@ bool make_page_map(const void* cache, int64_t block_stride, int64_t head_stride,
     return true;
 }
 
-template <int D, int BITS, int P, int NT, class IN, bool ROT>
+template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD>
 int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                    const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                    int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
-                   int32_t n_seqs, cudaStream_t stream) {
+                   int32_t n_seqs, const int32_t* order, cudaStream_t stream) {
     using C = MmaCfg<D, BITS, P, NT>;
-    auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT>;
+    auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT, ORD>;
     CUtensorMap map;
     memset(&map, 0, sizeof(map));
     uint32_t swz_m = 0;
@@ -786,7 +787,7 @@ int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t b
     launch_pdl(kern, grid, dim3(MMA_NW * WARP), C::SMEM, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
                static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
                block_table, seq_lens, max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml, part_o, map,
-               tma ? 1 : 0, swz_m, rows_per_head, box_rows);
+               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
@@ -794,14 +795,18 @@ template <int D, int BITS, int P, int NT, class IN>
 int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
-               int32_t n_seqs, int rot, cudaStream_t stream) {
-    if (rot)
-        return launch_mma_rot<D, BITS, P, NT, IN, true>(G, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
-                                                        block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml,
-                                                        part_o, n_seqs, stream);
-    return launch_mma_rot<D, BITS, P, NT, IN, false>(G, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
-                                                     block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml,
-                                                     part_o, n_seqs, stream);
+               int32_t n_seqs, int rot, const int32_t* order, cudaStream_t stream) {
+    if (rot)                                          // (the rotated decode runs in the natural order)
+        return launch_mma_rot<D, BITS, P, NT, IN, true, false>(G, q, out, cache, block_stride, head_stride, tail_k,
+                                                               tail_idx, block_table, seq_lens, max_pages, hkv, scale,
+                                                               n_splits, part_ml, part_o, n_seqs, nullptr, stream);
+    if (order)
+        return launch_mma_rot<D, BITS, P, NT, IN, false, true>(G, q, out, cache, block_stride, head_stride, tail_k,
+                                                               tail_idx, block_table, seq_lens, max_pages, hkv, scale,
+                                                               n_splits, part_ml, part_o, n_seqs, order, stream);
+    return launch_mma_rot<D, BITS, P, NT, IN, false, false>(G, q, out, cache, block_stride, head_stride, tail_k,
+                                                            tail_idx, block_table, seq_lens, max_pages, hkv, scale,
+                                                            n_splits, part_ml, part_o, n_seqs, nullptr, stream);
 }
 
 int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
@@ -813,7 +818,8 @@ int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
 int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
                       int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                       const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
-                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, cudaStream_t stream) {
+                      int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, const int32_t* order,
+                      cudaStream_t stream) {
     auto go = [&](auto Dc, auto Bc, auto Pc, auto in) -> int {
         using IN = decltype(in);
         if constexpr (std::is_same_v<IN, float>) {
@@ -821,16 +827,16 @@ int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, v
         } else if constexpr (Dc.value == 256) {
             return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                    tail_idx, block_table, seq_lens, max_pages, hkv,
-                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, stream);
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, order, stream);
         } else {
             if (G <= 8)
                 return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride,
                                                                        tail_k, tail_idx, block_table, seq_lens,
                                                                        max_pages, hkv, scale, n_splits, part_ml,
-                                                                       part_o, n_seqs, rot, stream);
+                                                                       part_o, n_seqs, rot, order, stream);
             return launch_mma<Dc.value, Bc.value, Pc.value, 2, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                    tail_idx, block_table, seq_lens, max_pages, hkv,
-                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, stream);
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, order, stream);
         }
     };
     return dispatch_fmt(D, bits, P, dtype, go);

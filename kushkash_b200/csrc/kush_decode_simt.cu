@@ -21,7 +21,8 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
-    float sm, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o, int rot) {
+    float sm, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o, int rot,
+    const int32_t* __restrict__ order) {
     using F = Fmt<D, BITS, P>;
     constexpr int NW = SIMT_NW;
     pdl_wait();                                            // previous kernel on the stream done
@@ -34,7 +35,7 @@ __global__ void __launch_bounds__(SIMT_NW * WARP) decode_simt_kernel(
     float* w_all = acc_all + NW * G * D;                   // [NW][G][P] scores -> weights
     float* st_all = w_all + NW * G * P;                    // [NW][3][G] m, l, vbacc
 
-    const int s = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
+    const int s = order ? order[blockIdx.x] : blockIdx.x, h = blockIdx.y, z = blockIdx.z;    // launch order
     const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP;
     const int64_t n = seq_lens[s];
     const int tail_n = int(n % P);
@@ -266,7 +267,7 @@ template <int D, int BITS, int P, class IN>
 int launch_decode_simt(const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                        const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                        int64_t max_pages, int32_t hkv, int32_t G, float scale, int32_t n_splits, float* part_ml,
-                       float* part_o, int32_t n_seqs, int rot, cudaStream_t stream) {
+                       float* part_o, int32_t n_seqs, int rot, const int32_t* order, cudaStream_t stream) {
     constexpr int NW = SIMT_NW;
     const size_t smem = sizeof(float) * (size_t(G) * D + 2 * size_t(NW) * G * D + size_t(NW) * G * P + 3 * size_t(NW) * G);
     if (smem > 200 * 1024) return set_error(KUSH_ERR_UNSUPPORTED, "decode: group %d too large for head_dim %d", G, D);
@@ -275,7 +276,7 @@ int launch_decode_simt(const void* q, void* out, const void* cache, int64_t bloc
     dim3 grid(n_seqs, hkv, n_splits);
     launch_pdl(kern, grid, dim3(NW * WARP), smem, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
                static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
-               block_table, seq_lens, max_pages, hkv, G, scale, n_splits, part_ml, part_o, rot);
+               block_table, seq_lens, max_pages, hkv, G, scale, n_splits, part_ml, part_o, rot, order);
     return check_launch("kush_sm100_decode (cuda cores)");
 }
 
@@ -293,11 +294,11 @@ int launch_decode_simt_any(int D, int bits, int P, int dtype, int G, const void*
                            int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                            const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv,
                            float scale, int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot,
-                           cudaStream_t stream) {
+                           const int32_t* order, cudaStream_t stream) {
     return dispatch_fmt(D, bits, P, dtype, [&](auto Dc, auto Bc, auto Pc, auto in) {
         return launch_decode_simt<Dc.value, Bc.value, Pc.value, decltype(in)>(
             q, out, cache, block_stride, head_stride, tail_k, tail_idx, block_table, seq_lens, max_pages, hkv, G,
-            scale, n_splits, part_ml, part_o, n_seqs, rot, stream);
+            scale, n_splits, part_ml, part_o, n_seqs, rot, order, stream);
     });
 }
 

@@ -449,3 +449,69 @@ extern "C" int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, i
                          page, dtype);
     return rc;
 }
+
+// ------------------------------------------------------------------ decode launch order
+namespace kush {
+
+constexpr int ORDER_KEYS = 4096;          // full-page counts above ORDER_KEYS - 1 share the top key
+
+// grid 1, block 1024: order[0..S) = the sequences by full pages, most first (a counting sort; ties in any order)
+__global__ void __launch_bounds__(1024) order_kernel(const int32_t* __restrict__ seq_lens, int S, int P,
+                                                     int32_t* __restrict__ order) {
+    pdl_wait();
+    __shared__ int cnt[ORDER_KEYS];
+    __shared__ int warp_tot[32];
+    constexpr int PER = ORDER_KEYS / 1024;                 // keys per thread, thread t: keys from the top down
+    const int tid = threadIdx.x, lane = tid % WARP, w = tid / WARP;
+    for (int i = tid; i < ORDER_KEYS; i += 1024) cnt[i] = 0;
+    __syncthreads();
+    auto key = [&](int s) { return min(max(seq_lens[s], 0) / P, ORDER_KEYS - 1); };
+    for (int s = tid; s < S; s += 1024) atomicAdd(&cnt[key(s)], 1);
+    __syncthreads();
+    // start of each key in descending key order: exclusive scan over the keys from ORDER_KEYS - 1 down to 0
+    int mine[PER], sum = 0;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        mine[j] = cnt[ORDER_KEYS - 1 - (tid * PER + j)];
+        sum += mine[j];
+    }
+    int incl = sum;                                        // inclusive scan of the per-thread sums
+#pragma unroll
+    for (int o = 1; o < WARP; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == WARP - 1) warp_tot[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        int t = warp_tot[lane], ti = t;
+#pragma unroll
+        for (int o = 1; o < WARP; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, ti, o);
+            if (lane >= o) ti += v;
+        }
+        warp_tot[lane] = ti - t;                           // exclusive prefix of the warp totals
+    }
+    __syncthreads();
+    int run = warp_tot[w] + incl - sum;                    // exclusive prefix of this thread's first key
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        cnt[ORDER_KEYS - 1 - (tid * PER + j)] = run;
+        run += mine[j];
+    }
+    __syncthreads();
+    for (int s = tid; s < S; s += 1024) order[atomicAdd(&cnt[key(s)], 1)] = s;
+}
+
+}  // namespace kush
+
+extern "C" int kush_sm100_order_longest_first(const int32_t* seq_lens, int32_t n_seqs, int32_t page, int32_t* order,
+                                              void* stream) {
+    if (n_seqs < 0 || page < 1) return set_error(KUSH_ERR_ARG, "kush_sm100_order_longest_first: n_seqs %d page %d",
+                                                 n_seqs, page);
+    if (n_seqs == 0) return KUSH_OK;
+    if (!seq_lens || !order) return set_error(KUSH_ERR_ARG, "kush_sm100_order_longest_first: null pointer");
+    launch_pdl(order_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), seq_lens, int(n_seqs),
+               int(page), order);
+    return check_launch("kush_sm100_order_longest_first");
+}

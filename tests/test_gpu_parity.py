@@ -179,6 +179,45 @@ def test_decode_ragged_splits(n_splits, dtype):
     assert_close(out, want, dtype, f"ragged splits={n_splits}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("n_splits", [1, 3])
+def test_decode_longest_first_order(n_splits, dtype):
+    """longest_first() is a permutation of the sequences by full pages, most first; a decode launched in that order
+    gives the natural-order decode's outputs bit for bit (bf16: tensor-core kernel, fp32: CUDA-core kernel)."""
+    D, bits, G, P, H = 128, 4, 4, 16, 2
+    g = torch.Generator().manual_seed(21)
+    lens = torch.randint(1, 40 * P, (37,), generator=g).tolist() + [0, 200 * P, 5 * P]
+    B = len(lens)
+    pages = max(-(-n // P) for n in lens)
+    bt = torch.randperm(B * pages, generator=g).to(torch.int32).view(B, pages)
+    ops = gpu_ops(D, bits, G, dtype, P)
+    st = make_state(B, H, D, bits, P, bt, B * pages, "cuda", dtype)
+    T = sum(lens)
+    k = torch.randn(T, H, D, generator=g).to("cuda", dtype)
+    v = torch.randn(T, H, D, generator=g).to("cuda", dtype)
+    qsl = torch.tensor([0] + lens, dtype=torch.int64).cumsum(0).to(torch.int32).cuda()
+    jobs = [(s, p) for s in range(B) for p in range(-(-lens[s] // P))]
+    js = torch.tensor([j[0] for j in jobs], dtype=torch.int32).cuda()
+    jp = torch.tensor([j[1] for j in jobs], dtype=torch.int32).cuda()
+    st.seq_lens.copy_(torch.tensor(lens, dtype=torch.int32))
+    ops.write(k, v, qsl, st.seq_lens, st.tail_idx, js, jp, st.pool, st.block_table, st.tail_k)
+    order = ops.longest_first(st.seq_lens).cpu()
+    assert sorted(order.tolist()) == list(range(B))
+    full = [lens[s] // P for s in order.tolist()]
+    assert full == sorted(full, reverse=True)
+    q = torch.randn(B, H * G, D, generator=g).to("cuda", dtype)
+    work = torch.empty(ops.work_size(B, H, n_splits), device="cuda")
+    outs = []
+    for o in (None, order.cuda()):
+        out = torch.full((B, H * G, D), float("nan"), dtype=dtype, device="cuda")
+        ops.decode(q, out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5, n_splits, work,
+                   order=o)
+        outs.append(out)
+    a, b = outs
+    assert torch.equal(a.view(torch.int16 if dtype != torch.float32 else torch.int32),
+                       b.view(torch.int16 if dtype != torch.float32 else torch.int32))
+
+
 def test_decode_tail_only_and_exact_page():
     for n in (1, 5, 31, 32, 33, 64):
         out, want, _ = decode_both(128, 4, 4, 32, 2, 2, n, torch.bfloat16)
