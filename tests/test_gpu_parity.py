@@ -218,6 +218,20 @@ def test_decode_longest_first_order(n_splits, dtype):
                        b.view(torch.int16 if dtype != torch.float32 else torch.int32))
 
 
+def test_longest_first_many_sequences():
+    """5000 sequences (more than the kernel's 1024 threads), lengths up to past the 4095-page top key: a permutation,
+    ranked by min(full pages, 4095) most first."""
+    g = torch.Generator().manual_seed(5)
+    P = 16
+    lens = torch.randint(0, 70000, (5000,), generator=g, dtype=torch.int32)
+    lens[:10] = 0
+    ops = gpu_ops(128, 4, 4, torch.bfloat16, P)
+    order = ops.longest_first(lens.cuda()).cpu().tolist()
+    assert sorted(order) == list(range(5000))
+    keys = [min(int(lens[s]) // P, 4095) for s in order]
+    assert keys == sorted(keys, reverse=True)
+
+
 def test_decode_tail_only_and_exact_page():
     for n in (1, 5, 31, 32, 33, 64):
         out, want, _ = decode_both(128, 4, 4, 32, 2, 2, n, torch.bfloat16)
