@@ -214,18 +214,7 @@ __global__ void __launch_bounds__(256) combine_kernel(IN* __restrict__ out, cons
     const int d = threadIdx.x;
     const float* ml = part_ml + (sh * n_splits * G + g) * 2;     // split z at ml[2 z G]
     const float* po = part_o + (sh * n_splits * G + g) * D + d;  // split z at po[z G D]
-    float M = -INFINITY;
-    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ml[2 * int64_t(z) * G]);
-    float L = 0.0f, o = 0.0f;
-    for (int z = 0; z < n_splits; z++) {
-        const float mz = ml[2 * int64_t(z) * G];
-        if (mz > -INFINITY) {
-            const float f = __expf(mz - M);
-            L = fmaf(ml[2 * int64_t(z) * G + 1], f, L);
-            o = fmaf(f, po[int64_t(z) * G * D], o);
-        }
-    }
-    out[(sh * G + g) * D + d] = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
+    out[(sh * G + g) * D + d] = from_f32<IN>(merge_splits(ml, po, n_splits, G, D));
 }
 
 // combine_kernel with the merged output rotated back (canonical FWHT) before its store: the row of D values goes
@@ -240,18 +229,7 @@ __global__ void __launch_bounds__(D) combine_rot_kernel(IN* __restrict__ out, co
     const int d = threadIdx.x;
     const float* ml = part_ml + (sh * n_splits * G + g) * 2;
     const float* po = part_o + (sh * n_splits * G + g) * D + d;
-    float M = -INFINITY;
-    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ml[2 * int64_t(z) * G]);
-    float L = 0.0f, o = 0.0f;
-    for (int z = 0; z < n_splits; z++) {
-        const float mz = ml[2 * int64_t(z) * G];
-        if (mz > -INFINITY) {
-            const float f = __expf(mz - M);
-            L = fmaf(ml[2 * int64_t(z) * G + 1], f, L);
-            o = fmaf(f, po[int64_t(z) * G * D], o);
-        }
-    }
-    row[d] = L > 0.0f ? o / L : 0.0f;
+    row[d] = merge_splits(ml, po, n_splits, G, D);
     __syncthreads();
     if (d < WARP) {
         float x[D / WARP];

@@ -53,18 +53,7 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(IN* const* __restri
     const int d = threadIdx.x;
     const float* ml = part_ml + (sh * n_splits * G + g) * 2;
     const float* po = part_o + (sh * n_splits * G + g) * D + d;
-    float M = -INFINITY;
-    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ml[2 * int64_t(z) * G]);
-    float L = 0.0f, o = 0.0f;
-    for (int z = 0; z < n_splits; z++) {
-        const float mz = ml[2 * int64_t(z) * G];
-        if (mz > -INFINITY) {
-            const float f = __expf(mz - M);
-            L = fmaf(ml[2 * int64_t(z) * G + 1], f, L);
-            o = fmaf(f, po[int64_t(z) * G * D], o);
-        }
-    }
-    const IN v = from_f32<IN>(L > 0.0f ? o / L : 0.0f);
+    const IN v = from_f32<IN>(merge_splits(ml, po, n_splits, G, D));
     const int64_t at = (s * hq_total + (int64_t(rank) * H + h) * G + g) * D + d;
     for (int r = 0; r < world; r++) outs[r][at] = v;
     __syncthreads();
