@@ -148,11 +148,12 @@ int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page, int32_t d
                          int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o,
                          int32_t n_seqs, int32_t flags, const int32_t *order, void *stream);
 
-/* The decode of kush_sm100_decode with a stream partition of the work instead of split-KV: the pages of all
- * (sequence, kv head) units laid end to end (a unit's full pages, then its tail page when it has one) are cut into
- * n_ctas equal ranges, one CTA each, so every CTA reads the same number of pages however ragged seq_lens is.  A unit
- * inside one range is written to out by its CTA; the pieces of a unit cut across ranges go to partials in `work` and
- * a combine merges them (split-KV's merge).  Three launches on `stream` (a one-CTA prefix sum of the sequences' page
+/* The decode of kush_sm100_decode with a stream partition of the work instead of split-KV: for each kv head the
+ * pages of the sequences (a sequence's full pages, then its tail page when it has one) laid end to end are cut into
+ * n_ctas / hkv equal ranges, one CTA each, so every CTA reads the same number of pages however ragged seq_lens is
+ * (n_ctas must be a multiple of hkv; the CTAs of all kv heads with the same range read the same blocks together).
+ * A (sequence, kv head) inside one range is written to out by its CTA; the pieces of one cut across ranges go to
+ * partials in `work` and a combine merges them (split-KV's merge).  Three launches on `stream` (a one-CTA prefix sum of the sequences' page
  * counts, the decode, the combine); no host synchronisation.  work: fp32, at least kush_sm100_decode_stream_work
  * elements, 16-byte aligned.  Tensor-core configurations only (KUSH_ERR_UNSUPPORTED otherwise).  Outputs agree with
  * kush_sm100_decode within fp32 reassociation of the merge.  No counterpart in the reference (an extension over

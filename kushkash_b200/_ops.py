@@ -189,9 +189,9 @@ class Ops:
                                                                n_splits, H)
 
     def stream_ctas(self, num_seqs: int, num_kv_heads: int, max_full_pages: int) -> int:
-        """CTAs for decode_stream: one wave of the stream decode kernel on this device, fewer when the batch holds under
-        MIN_STREAM_PAGES pages per CTA (counting num_seqs x num_kv_heads x (max_full_pages + 1) pages, an upper
-        bound).  No counterpart in the reference."""
+        """CTAs for decode_stream, a multiple of num_kv_heads: one wave of the stream decode kernel on this device,
+        fewer when the batch holds under MIN_STREAM_PAGES pages per CTA (counting num_seqs x (max_full_pages + 1)
+        pages per kv head, an upper bound).  No counterpart in the reference."""
         if getattr(self, "_wave", None) is None:
             from . import _cuda
             c = self.cfg
@@ -200,8 +200,8 @@ class Ops:
             if wave <= 0:
                 _cuda.check(wave, "kush_sm100_decode_stream_ctas")
             self._wave = wave
-        pages = num_seqs * num_kv_heads * (max_full_pages + 1)
-        return max(1, min(self._wave, -(-pages // MIN_STREAM_PAGES)))
+        ranges = min(self._wave // num_kv_heads, -(-num_seqs * (max_full_pages + 1) // MIN_STREAM_PAGES))
+        return max(1, ranges) * num_kv_heads
 
     def stream_work_size(self, num_seqs: int, num_kv_heads: int, n_ctas: int) -> int:
         """fp32 elements of decode_stream's work buffer: (S * Hkv + n_ctas) * G * (D + 2) partials and S + 1 + n_ctas
@@ -211,9 +211,9 @@ class Ops:
     def decode_stream(self, q: torch.Tensor, out: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                       seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float, n_ctas: int,
                       work: torch.Tensor) -> None:
-        """decode() with the stream partition in place of split-KV (an extension): the pages of all (sequence, kv
-        head) units cut into n_ctas equal ranges, so a ragged batch loads every CTA alike (stream_ctas() picks
-        n_ctas).  Same outputs as decode() up to fp32 reassociation of the merge.  work: contiguous fp32 of at least
+        """decode() with the stream partition in place of split-KV (an extension): each kv head's pages of all
+        sequences cut into n_ctas / Hkv equal ranges (n_ctas a multiple of Hkv), so a ragged batch loads every CTA
+        alike (stream_ctas() picks n_ctas).  Same outputs as decode() up to fp32 reassociation of the merge.  work: contiguous fp32 of at least
         stream_work_size(S, Hkv, n_ctas) elements.  Tensor-core configurations only (ValueError otherwise)."""
         S, H = q.shape[0], tail_k.shape[1]
         need = self.stream_work_size(S, H, n_ctas)

@@ -314,13 +314,14 @@ constexpr float TAU = 4.0f;
 
 // grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store;
 // ORD: CTA x works on sequence order[x] (separate instantiations, so the plain kernels keep their code).
-// STR (stream partition): grid (C); the pages of all (sequence, kv head) units laid end to end (unit s Hkv + h holds
-// the sequence's full pages, then one more for its tail page when it has one) and cut into C equal ranges, CTA c
-// taking range c one unit segment at a time (the body below runs once per segment; without STR once).  spre =
-// [pre[0..S] | start[0..C)]: pre the exclusive prefix sums of the sequences' page counts, start[c] the sequence
-// holding range c's first page (stream_prep_kernel).  A unit wholly inside one range is written to out; the segment
-// of unit u in range c is partial u + c (a unit's partials are contiguous: the ranges after c start at later units),
-// merged by combine_stream_kernel.
+// STR (stream partition): grid (Hkv R); for each kv head, the pages of its units (sequence s: its full pages, then
+// one more for its tail page when it has one) laid end to end in sequence order and cut into R equal ranges, CTA
+// h R + r taking range r of head h one sequence segment at a time (the body below runs once per segment; without
+// STR once).  The CTAs of all kv heads with the same r read the same blocks at the same time, as split-KV's do.
+// spre = [pre[0..S] | start[0..R)]: pre the exclusive prefix sums of the sequences' page counts, start[r] the
+// sequence holding range r's first page (stream_prep_kernel).  A unit wholly inside one range is written to out; the
+// segment of (s, h) in range r is partial h (S + R) + s + r (a unit's partials are contiguous: the ranges after r
+// start at later sequences), merged by combine_stream_kernel.
 template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD, bool STR = false>
 __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB)) decode_mma_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
@@ -343,18 +344,22 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     float* kbr = qsm + G * D;                                           // [D] kb_ref
     __half* kb16 = reinterpret_cast<__half*>(kbr + D);                  // [D] kb_ref as fp16 (read in K pair order)
     const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP, g = lane >> 2, tid = lane & 3;
-    // STR: this CTA's page range [f, fend) of the T pages of all units, the sequence sq holding page f, the parity
-    // of each of this warp's ring slots (kept across segments), and whether a copy ever failed to complete
+    // STR: this CTA's kv head hs and range rr (of nr per head), its pages [f, fend) of the head's pages, the
+    // sequence sq holding page f, the parity of each of this warp's ring slots (kept across segments), and whether a
+    // copy ever failed to complete
     int64_t f = 0, fend = 0, ppc = 1;
-    int sq = 0;
+    int sq = 0, hs = 0, rr = 0, nr = 1;
     uint32_t phase = 0;
     bool dead = false;
     if constexpr (STR) {
-        const int64_t T = int64_t(H) * spre[n_seqs];
-        ppc = (T + gridDim.x - 1) / gridDim.x;
-        f = int64_t(blockIdx.x) * ppc;
-        fend = min(T, f + ppc);
-        sq = f < T ? spre[n_seqs + 1 + blockIdx.x] : 0;
+        nr = int(gridDim.x) / H;
+        hs = int(blockIdx.x) / nr;
+        rr = int(blockIdx.x) % nr;
+        const int64_t Th = spre[n_seqs];
+        ppc = (Th + nr - 1) / nr;
+        f = int64_t(rr) * ppc;
+        fend = min(Th, f + ppc);
+        sq = f < Th ? spre[n_seqs + 1 + rr] : 0;
         if (threadIdx.x == 0) {
             for (int i = 0; i < NW * NS; i++) mbar_init(&bars[i], 1);
             fence_mbar_init();                        // (published by the first segment's barrier)
@@ -367,15 +372,10 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     bool whole = false;                               // STR: the unit lies in this range alone
     if constexpr (STR) {
         if (f >= fend) return;
-        int64_t ub = int64_t(H) * spre[sq], ue = int64_t(H) * spre[sq + 1];
-        while (ue <= f) {                             // (sequences without tokens hold no pages)
-            sq++;
-            ub = ue;
-            ue = int64_t(H) * spre[sq + 1];
-        }
-        const int64_t ln = (ue - ub) / H, us = ub + (f - ub) / ln * ln;   // pages of a unit, the unit's first page
+        while (spre[sq + 1] <= f) sq++;               // (sequences without tokens hold no pages)
+        const int64_t us = spre[sq], ln = spre[sq + 1] - us;   // the unit's first page and its pages
         s = sq;
-        h = int((f - ub) / ln);
+        h = hs;
         z = 0;
         seg0 = f - us;
         seg1 = min(ln, seg0 + (fend - f));
@@ -760,7 +760,8 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
         if (STR ? whole : n_splits == 1) {
             out[qbase + idx] = from_f32<IN>(Ls > 0.0f ? acc / Ls : (ok ? 0.0f : NAN));
         } else {
-            const int64_t pb = (STR ? int64_t(s) * H + h + blockIdx.x : (int64_t(s) * H + h) * n_splits + z) * G + hd;
+            const int64_t pb =
+                (STR ? int64_t(h) * (n_seqs + nr) + s + rr : (int64_t(s) * H + h) * n_splits + z) * G + hd;
             part_o[pb * D + d] = acc;
             if (d == 0) {
                 part_ml[pb * 2] = M * 0.69314718055994531f;           // log2 units -> natural, for the combine
@@ -869,11 +870,11 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
 }
 
 // ------------------------------------------------------------------ stream partition: prep and combine
-// one CTA of 1024 threads: spre = [pre[0..S] | start[0..C)] for decode_mma_kernel<..., STR>: pre[s] the pages of
-// the sequences before s (a sequence's full pages plus one for a partial tail page), start[c] the last sequence s with
-// H pre[s] <= c ppc (the sequence holding range c's first page; 0 for an empty range), ppc = ceil(H pre[S] / C)
+// one CTA of 1024 threads: spre = [pre[0..S] | start[0..R)] for decode_mma_kernel<..., STR>: pre[s] the pages of
+// the sequences before s (a sequence's full pages plus one for a partial tail page), start[r] the last sequence s with
+// pre[s] <= r ppc (the sequence holding range r's first page; 0 for an empty range), ppc = ceil(pre[S] / R)
 __global__ void __launch_bounds__(1024) stream_prep_kernel(const int32_t* __restrict__ seq_lens, int n_seqs, int P,
-                                                           int H, int n_ctas, int32_t* __restrict__ spre) {
+                                                           int n_ranges, int32_t* __restrict__ spre) {
     __shared__ int32_t wsum[32];
     __shared__ int32_t carry;
     pdl_wait();                                       // previous kernel on the stream done (it may append tokens)
@@ -913,26 +914,27 @@ __global__ void __launch_bounds__(1024) stream_prep_kernel(const int32_t* __rest
         if (t == 1023) carry = incl;
         __syncthreads();
     }
-    const int64_t T = int64_t(H) * carry, ppc = (T + n_ctas - 1) / n_ctas;
-    for (int c = t; c < n_ctas; c += 1024) {
-        const int64_t f = int64_t(c) * ppc;
+    const int64_t T = carry, ppc = (T + n_ranges - 1) / n_ranges;
+    for (int r = t; r < n_ranges; r += 1024) {
+        const int64_t f = int64_t(r) * ppc;
         int lo = 0;
         if (f < T) {
             int hi = n_seqs - 1;
             while (lo < hi) {
                 const int mid = (lo + hi + 1) / 2;
-                if (int64_t(H) * spre[mid] <= f)
+                if (spre[mid] <= f)
                     lo = mid;
                 else
                     hi = mid - 1;
             }
         }
-        spre[n_seqs + 1 + c] = lo;
+        spre[n_seqs + 1 + r] = lo;
     }
 }
 
-// grid (S Hkv G), block D: the output of (unit u = s Hkv + h, group head g) from its partials u + c0 .. u + c1 (the
-// ranges c0..c1 its pages span); a unit inside one range was written by the decode, one without pages gets zeros
+// grid (S Hkv G), block D: the output of (sequence s, kv head h, group head g) from its partials h (S + R) + s + r,
+// r = r0..r1 (the ranges its pages span); a unit inside one range was written by the decode, one without pages gets
+// zeros
 template <class IN>
 __global__ void __launch_bounds__(256) combine_stream_kernel(IN* __restrict__ out, const float* __restrict__ part_ml,
                                                              const float* __restrict__ part_o,
@@ -947,10 +949,11 @@ __global__ void __launch_bounds__(256) combine_stream_kernel(IN* __restrict__ ou
         *o = from_f32<IN>(0.0f);
         return;
     }
-    const int64_t T = int64_t(H) * spre[n_seqs], ppc = (T + n_ctas - 1) / n_ctas;
-    const int64_t us = int64_t(H) * spre[s] + h * ln, c0 = us / ppc, c1 = (us + ln - 1) / ppc;
+    const int nr = n_ctas / H;
+    const int64_t ppc = (int64_t(spre[n_seqs]) + nr - 1) / nr;
+    const int64_t us = spre[s], c0 = us / ppc, c1 = (us + ln - 1) / ppc;
     if (c0 == c1) return;
-    const int64_t first = u + c0;
+    const int64_t first = int64_t(h) * (n_seqs + nr) + s + c0;
     *o = from_f32<IN>(merge_splits(part_ml + (first * G + g) * 2, part_o + (first * G + g) * D + d, int(c1 - c0 + 1),
                                    G, D));
 }
@@ -1057,9 +1060,9 @@ extern "C" int kush_sm100_decode_stream(int32_t head_dim, int32_t bits, int32_t 
                                         const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages,
                                         int32_t hkv, float scale, int32_t n_ctas, float* work, int64_t work_elems,
                                         int32_t n_seqs, void* stream) {
-    if (n_seqs < 0 || hkv < 1 || group < 1 || n_ctas < 1 || n_ctas > (1 << 30))
-        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_stream: n_seqs %d hkv %d group %d n_ctas %d", n_seqs, hkv,
-                         group, n_ctas);
+    if (n_seqs < 0 || hkv < 1 || group < 1 || n_ctas < 1 || n_ctas > (1 << 30) || n_ctas % hkv)
+        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_stream: n_seqs %d hkv %d group %d n_ctas %d (a multiple of "
+                                       "hkv)", n_seqs, hkv, group, n_ctas);
     if (n_seqs == 0) return KUSH_OK;
     if (kush_sm100_record_bytes(head_dim, bits, page) == 0 || !decode_mma_supported(head_dim, bits, page, dtype, group))
         return set_error(KUSH_ERR_UNSUPPORTED, "kush_sm100_decode_stream: head_dim %d bits %d page %d dtype %d group "
@@ -1078,7 +1081,7 @@ extern "C" int kush_sm100_decode_stream(int32_t head_dim, int32_t bits, int32_t 
     float* part_o = work + parts * 2;
     int32_t* spre = reinterpret_cast<int32_t*>(part_o + parts * head_dim);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    launch_pdl(stream_prep_kernel, dim3(1), dim3(1024), 0, st, seq_lens, n_seqs, int(page), int(hkv), int(n_ctas), spre);
+    launch_pdl(stream_prep_kernel, dim3(1), dim3(1024), 0, st, seq_lens, n_seqs, int(page), int(n_ctas / hkv), spre);
     int rc = check_launch("kush_sm100_decode_stream (prep)");
     if (rc != KUSH_OK) return rc;
     rc = decode_stream_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,

@@ -215,19 +215,19 @@ STREAM_GEOMETRIES = [(128, 8, 7, 32, 4), (128, 4, 4, 16, 2), (128, 4, 4, 32, 2),
 
 
 @pytest.mark.parametrize("D,bits,G,P,H", STREAM_GEOMETRIES)
-@pytest.mark.parametrize("n_ctas", [1, 5, 37, 0])
-def test_decode_stream(D, bits, G, P, H, n_ctas):
+@pytest.mark.parametrize("ranges", [1, 5, 37, 0])
+def test_decode_stream(D, bits, G, P, H, ranges):
     """The stream partition on a ragged batch (0 tokens .. 200 pages, tail-only, page-aligned) gives the oracle's
-    outputs at every CTA count: one range (every unit a segment of one CTA, written directly), a few ranges (units
-    cut across CTAs, merged by the combine), and stream_ctas() (0 here); the work buffer and outputs start as NaN, so a
-    partial or output left unwritten fails."""
+    outputs at every range count per kv head: one range (every sequence a segment of one CTA, written directly), a
+    few ranges (sequences cut across CTAs, merged by the combine), and stream_ctas() (0 here); the work buffer and
+    outputs start as NaN, so a partial or output left unwritten fails."""
     from kushkash_b200._cuda import device_error
     lens = [0, 1, 9, P, 3 * P + 5, 40 * P + 7, 200 * P, 17 * P + 15, 64 * P + 1]
     go, st, ro, ref, q = ragged_state(D, bits, G, P, H, lens, 31)
     B = len(lens)
     want = torch.empty(B, H * G, D)
     ro.decode(q.contiguous(), want, ref.pool, ref.block_table, ref.seq_lens, ref.tail_idx, ref.tail_k, D ** -0.5)
-    C = n_ctas or go.stream_ctas(B, H, max(lens) // P)
+    C = ranges * H or go.stream_ctas(B, H, max(lens) // P)
     out = torch.full((B, H * G, D), float("nan"), dtype=torch.bfloat16, device="cuda")
     work = torch.full((go.stream_work_size(B, H, C),), float("nan"), device="cuda")
     go.decode_stream(q.to("cuda", torch.bfloat16).contiguous(), out, st.pool, st.block_table, st.seq_lens, st.tail_idx,
@@ -238,7 +238,7 @@ def test_decode_stream(D, bits, G, P, H, n_ctas):
 
 def test_decode_stream_many_sequences():
     """1500 short sequences (0 .. 3 pages: the prefix sum runs over two 1024-sequence blocks) and one long one, at a
-    wave of CTAs and at 3: the stream decode agrees with the split-KV decode (itself held to the oracle above) within
+    wave of CTAs and at 3 ranges per kv head: the stream decode agrees with the split-KV decode (itself held to the oracle above) within
     the merge's fp32 reassociation."""
     D, bits, G, P, H = 128, 4, 4, 16, 2
     g = torch.Generator().manual_seed(41)
@@ -248,7 +248,7 @@ def test_decode_stream_many_sequences():
     qd = q.to("cuda", torch.bfloat16).contiguous()
     want = torch.empty(B, H * G, D, dtype=torch.bfloat16, device="cuda")
     go.decode(qd, want, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5)
-    for C in (go.stream_ctas(B, H, max(lens) // P), 3):
+    for C in (go.stream_ctas(B, H, max(lens) // P), 3 * H):
         out = torch.full_like(want, float("nan"))
         work = torch.full((go.stream_work_size(B, H, C),), float("nan"), device="cuda")
         go.decode_stream(qd, out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5, C, work)
