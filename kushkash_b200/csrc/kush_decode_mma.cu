@@ -295,7 +295,11 @@ struct MmaCfg {
     static constexpr int NS = RB <= 3072 ? 4 : 2;
     static constexpr int GMAX = 8 * NT;
     static constexpr int MERGE = 4 * ((MMA_NW + 1) * GMAX * D + 2 * (MMA_NW + 1) * GMAX);
-    static constexpr int RING = MMA_NW * NS * RB > MERGE ? MMA_NW * NS * RB : (MERGE + 127) / 128 * 128;
+    // after the merge area: the tail page's record from its V code rows on (V rows, then at their record offsets the
+    // V scales and biases), staged for the tail partial
+    static constexpr int TSTAGE = (MERGE + 15) / 16 * 16;
+    static constexpr int TEND = TSTAGE + RB - Fmt<D, BITS, P>::OFF_VQ;
+    static constexpr int RING = MMA_NW * NS * RB > TEND ? MMA_NW * NS * RB : (TEND + 127) / 128 * 128;
     static constexpr int BARS = (8 * MMA_NW * NS + 127) / 128 * 128;
     // shared memory: [bars | pad to 1024 | ring: int8 code slots [NW][NS][CODES] + scale slots [NW][NS][SCALES], int4
     // record slots [NW][NS][RB] (reused by the merge) | q * scale (fp32, [G][D]) | kb_ref (fp32, [D]) | kb_ref (fp16,
@@ -314,8 +318,9 @@ constexpr float TAU = 4.0f;
 
 // grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store;
 // ORD: CTA x works on sequence order[x] (separate instantiations, so the plain kernels keep their code).
-// STR (stream partition): grid (Hkv R); for each kv head, the pages of its units (sequence s: its full pages, then
-// one more for its tail page when it has one) laid end to end in sequence order and cut into R equal ranges, CTA
+// STR (stream partition): grid (Hkv R); for each kv head, the positions of its units (sequence s with tokens:
+// `setup` positions standing for the fixed cost of a segment, its full pages, then one more for its tail page when it
+// has one) laid end to end in sequence order and cut into R equal ranges, CTA
 // h R + r taking range r of head h one sequence segment at a time (the body below runs once per segment; without
 // STR once).  The CTAs of all kv heads with the same r read the same blocks at the same time, as split-KV's do.
 // spre = [pre[0..S] | start[0..R)]: pre the exclusive prefix sums of the sequences' page counts, start[r] the
@@ -329,7 +334,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
     float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o,
     const __grid_constant__ CUtensorMap tmap, int use_tma, uint32_t swz_m, int32_t rows_per_head, int32_t box_rows,
-    const int32_t* __restrict__ order, const int32_t* __restrict__ spre, int n_seqs) {
+    const int32_t* __restrict__ order, const int32_t* __restrict__ spre, int n_seqs, int setup) {
     static_assert(!(STR && (ROT || ORD)), "the stream partition runs unrotated in its own order");
     using F = Fmt<D, BITS, P>;
     using L = Lay<D, BITS>;
@@ -381,6 +386,8 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
         seg1 = min(ln, seg0 + (fend - f));
         whole = us / ppc == (us + ln - 1) / ppc;
         f += seg1 - seg0;
+        seg0 = max(seg0 - setup, int64_t(0));          // positions -> pages (a sequence's first `setup` positions
+        seg1 = max(seg1 - setup, int64_t(0));          // stand for its setup cost and hold no page)
     } else {
         s = ORD ? order[blockIdx.x] : blockIdx.x;     // launch order
         h = blockIdx.y;
@@ -675,6 +682,17 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
         const IN* tk = has_tail ? tail_k + ((int64_t(tail_idx[s]) * H + h) * P + min(lane, P - 1)) * D : nullptr;
         const uint8_t* trec = has_tail ? hcache + int64_t(bt[full]) * block_stride : nullptr;
         constexpr int R = D / WARP;
+        // the record's V rows [0, tail_n) and its V scales and biases into shared memory, all 16-byte loads in flight
+        // at once (read per token from global memory, the tail cost one round trip per token)
+        uint8_t* tv = ring + C::TSTAGE;
+        if (has_tail) {
+            const int nv = tail_n * F::DC / 16;
+            for (int i = threadIdx.x; i < nv + P / 4; i += NW * WARP) {
+                const int off = i < nv ? F::OFF_VQ + 16 * i : F::OFF_VS + 16 * (i - nv);
+                *reinterpret_cast<uint4*>(tv + off - F::OFF_VQ) = *reinterpret_cast<const uint4*>(trec + off);
+            }
+        }
+        __syncthreads();
         for (int hd = wid; hd < G; hd += NW) {
             const float* qh = qsm + hd * D;
             float qkref = 0.0f;                                          // q . kb_ref (the shift of every score)
@@ -704,10 +722,10 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             for (int i = 0; i < R; i++) acc[i] = 0.0f;
             for (int t = 0; t < tail_n && has_tail; t++) {               // lane holds dims lane + 32 i
                 const float pt = __shfl_sync(0xffffffffu, p, t);
-                const float vs = h_load(trec + F::OFF_VS, t) * pt, vb = h_load(trec + F::OFF_VB, t) * pt;
+                const float vs = h_load(tv + F::OFF_VS - F::OFF_VQ, t) * pt, vb = h_load(tv + F::OFF_VB - F::OFF_VQ, t) * pt;
 #pragma unroll
                 for (int i = 0; i < R; i++)
-                    acc[i] = fmaf(float(code_at<D, BITS>(trec + F::OFF_VQ + t * F::DC, lane + WARP * i)), vs, acc[i] + vb);
+                    acc[i] = fmaf(float(code_at<D, BITS>(tv + t * F::DC, lane + WARP * i)), vs, acc[i] + vb);
             }
 #pragma unroll
             for (int i = 0; i < R; i++) c_acc[(NW * G + hd) * D + lane + WARP * i] = acc[i];
@@ -825,7 +843,7 @@ int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t b
                    const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                    int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
                    int32_t n_seqs, const int32_t* order, cudaStream_t stream, const int32_t* spre = nullptr,
-                   int32_t n_ctas = 0) {
+                   int32_t n_ctas = 0, int32_t setup = 0) {
     using C = MmaCfg<D, BITS, P, NT>;
     auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT, ORD, STR>;
     CUtensorMap map;
@@ -847,7 +865,7 @@ int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t b
     launch_pdl(kern, grid, dim3(MMA_NW * WARP), C::SMEM, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
                static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
                block_table, seq_lens, max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml, part_o, map,
-               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order, spre, n_seqs);
+               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order, spre, n_seqs, setup);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
@@ -870,11 +888,15 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
 }
 
 // ------------------------------------------------------------------ stream partition: prep and combine
-// one CTA of 1024 threads: spre = [pre[0..S] | start[0..R)] for decode_mma_kernel<..., STR>: pre[s] the pages of
-// the sequences before s (a sequence's full pages plus one for a partial tail page), start[r] the last sequence s with
+// positions charged to each sequence for the fixed cost of a segment (q, kb_ref, pipeline fill, merge, tail)
+constexpr int STREAM_SETUP_PAGES = 32;
+
+// one CTA of 1024 threads: spre = [pre[0..S] | start[0..R)] for decode_mma_kernel<..., STR>: pre[s] the positions of
+// the sequences before s (a sequence with tokens: `setup`, its full pages, one for a partial tail page), start[r] the
+// last sequence s with
 // pre[s] <= r ppc (the sequence holding range r's first page; 0 for an empty range), ppc = ceil(pre[S] / R)
 __global__ void __launch_bounds__(1024) stream_prep_kernel(const int32_t* __restrict__ seq_lens, int n_seqs, int P,
-                                                           int n_ranges, int32_t* __restrict__ spre) {
+                                                           int n_ranges, int setup, int32_t* __restrict__ spre) {
     __shared__ int32_t wsum[32];
     __shared__ int32_t carry;
     pdl_wait();                                       // previous kernel on the stream done (it may append tokens)
@@ -889,7 +911,7 @@ __global__ void __launch_bounds__(1024) stream_prep_kernel(const int32_t* __rest
         int v = 0;
         if (s < n_seqs) {
             const int n = seq_lens[s];
-            v = n / P + (n % P != 0 ? 1 : 0);
+            v = n > 0 ? setup + n / P + (n % P != 0 ? 1 : 0) : 0;
         }
 #pragma unroll
         for (int o = 1; o < WARP; o <<= 1) {
@@ -982,7 +1004,7 @@ int decode_stream_mma(int D, int bits, int P, int dtype, int G, const void* q, v
             if (per_sm) return stream_resident_per_sm<Dc.value, Bc.value, Pc.value, NT, IN>(per_sm);
             return launch_mma_rot<Dc.value, Bc.value, Pc.value, NT, IN, false, false, true>(
                 G, q, out, cache, block_stride, head_stride, tail_k, tail_idx, block_table, seq_lens, max_pages, hkv,
-                scale, 1, part_ml, part_o, n_seqs, nullptr, stream, spre, n_ctas);
+                scale, 1, part_ml, part_o, n_seqs, nullptr, stream, spre, n_ctas, STREAM_SETUP_PAGES);
         };
         if constexpr (std::is_same_v<IN, float>) {
             return KUSH_ERR_UNSUPPORTED;
@@ -1081,7 +1103,8 @@ extern "C" int kush_sm100_decode_stream(int32_t head_dim, int32_t bits, int32_t 
     float* part_o = work + parts * 2;
     int32_t* spre = reinterpret_cast<int32_t*>(part_o + parts * head_dim);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    launch_pdl(stream_prep_kernel, dim3(1), dim3(1024), 0, st, seq_lens, n_seqs, int(page), int(n_ctas / hkv), spre);
+    launch_pdl(stream_prep_kernel, dim3(1), dim3(1024), 0, st, seq_lens, n_seqs, int(page), int(n_ctas / hkv),
+               int(STREAM_SETUP_PAGES), spre);
     int rc = check_launch("kush_sm100_decode_stream (prep)");
     if (rc != KUSH_OK) return rc;
     rc = decode_stream_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
