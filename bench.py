@@ -430,9 +430,6 @@ def main() -> None:
     ap.add_argument("--launch-order", choices=["longest", "natural"], default="longest",
                     help="ragged workloads (configs 2, 5): decode CTAs take the sequences longest first (an order "
                          "computed once per step) or in their natural order")
-    ap.add_argument("--partition", choices=["split", "stream"], default="split",
-                    help="ragged workloads (configs 1, 2, 5): decode work cut per sequence into split-KV splits, or "
-                         "the pages of all (sequence, kv head) units cut into equal ranges, one per CTA (stream)")
     ap.add_argument("--rotate", choices=["none", "fused", "unfused"], default="none",
                     help="config 3 with the Walsh-Hadamard rotation of kushkash's 4-bit default: inside the append and "
                          "decode kernels (fused) or as fwht launches around them (unfused); BASELINE runs without")
@@ -762,7 +759,7 @@ class RaggedEngine:
     of every sequence) for the write roofline."""
 
     def __init__(self, cfg: dict, lens: list[int], n_prompts: int, device: torch.device, seed: int,
-                 extra_tokens: int, keep_fill: bool, launch_order: str = "natural", partition: str = "split"):
+                 extra_tokens: int, keep_fill: bool, launch_order: str = "natural"):
         from kushkash_b200 import Ops
         self.dev, self.L, self.lens, self.PR = device, cfg["layers"], lens, n_prompts
         self.D, self.HKV, self.HQ, self.bits, self.P = 128, cfg["hkv"], cfg["hq"], cfg["bits"], cfg["P"]
@@ -794,10 +791,6 @@ class RaggedEngine:
         self.scale = 1.0 / math.sqrt(D)
         self.ns = self.ops.splits(S, H, max(lens) // P) if S else 1
         self.work = torch.empty(max(1, self.ops.work_size(max(S, 1), H, self.ns)), device=device)
-        self.n_ctas = 0                                # stream partition: CTAs of the decode (0: split-KV)
-        if partition == "stream" and S:
-            self.n_ctas = self.ops.stream_ctas(S, H, (max(lens) + extra_tokens) // P)
-            self.work = torch.empty(self.ops.stream_work_size(S, H, self.n_ctas), device=device)
         dgen = torch.Generator(device=device).manual_seed(seed + 1)
         self.fill_in = None
         self._fill(dgen, keep_fill)
@@ -817,7 +810,7 @@ class RaggedEngine:
         # layers share lengths); measured: config 5 (16k CTAs) step -4%, config 2 (512 CTAs, one wave) no gain
         self.order = None
         waves = S * H * self.ns / (4 * torch.cuda.get_device_properties(device).multi_processor_count)
-        if launch_order == "longest" and S > 1 and min(lens) != max(lens) and waves > 2 and not self.n_ctas:
+        if launch_order == "longest" and S > 1 and min(lens) != max(lens) and waves > 2:
             self.order = torch.empty(S, dtype=torch.int32, device=device)
 
     def _jobs(self, seqs: list[int]):
@@ -871,10 +864,6 @@ class RaggedEngine:
                        self.pool[layer], self.bt_pr, self.tail_pr[layer])
 
     def decode(self, layer: int) -> None:
-        if self.n_ctas:
-            self.ops.decode_stream(self.q[layer], self.out[layer], self.pool[layer], self.bt_dec, self.sl_dec[layer],
-                                   self.ti_dec, self.tail_dec[layer], self.scale, self.n_ctas, self.work)
-            return
         self.ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.bt_dec, self.sl_dec[layer], self.ti_dec,
                         self.tail_dec[layer], self.scale, self.ns, self.work, order=self.order)
 
@@ -918,8 +907,8 @@ class RaggedEngine:
         return self.S * self.HKV * (4 * self.D + self.DC + 4 + 2 * self.D)
 
     def launches_per_step(self) -> int:
-        dec = 3 if self.n_ctas else 1 + (1 if self.ns > 1 else 0)     # stream: prefix sum, decode, combine
-        return self.L * ((1 if self.PR else 0) + ((1 + dec) if self.S else 0)) + (1 if self.order is not None else 0)
+        return (self.L * ((1 if self.PR else 0) + ((2 + (1 if self.ns > 1 else 0)) if self.S else 0))
+                + (1 if self.order is not None else 0))
 
 
 def time_graph(gr, dev, reps: int = 3) -> float:
@@ -1023,7 +1012,7 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
     lens = [lens_all[i] for i in mine]
     n_pr = cfg["prompts"] // world
     eng = RaggedEngine(cfg, lens, n_pr, dev, seed=cfg["seed"] * 100 + rank, extra_tokens=a.warmup + 2 * a.steps + 8,
-                       keep_fill=n_pr == 0, launch_order=a.launch_order, partition=a.partition)
+                       keep_fill=n_pr == 0, launch_order=a.launch_order)
     kern = {}
     if n_pr == 0:                                   # write roofline: layer 0's whole contexts again
         wgraph = capture(eng.rewrite, dev)
@@ -1120,8 +1109,6 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
                        "q_heads": cfg["hq"], "kv_heads": cfg["hkv"], "head_dim": 128,
                        "parallelism": f"requests partitioned over {world} GPU(s) by tokens, no collective in the step",
                        "launch_order": "longest first" if eng.order is not None else "natural",
-                       "decode_partition": (f"stream ({eng.n_ctas} CTAs, equal page ranges)" if eng.n_ctas
-                                            else f"split-KV ({eng.ns} splits)"),
                        "l2": ("inputs larger than L2 (GBs of records per layer-step, no flush needed)" if which == "mix"
                               else "inputs smaller than L2: the graph replays re-read L2-resident records (launch- "
                                    "and latency-bound sizes, as the config intends)")},

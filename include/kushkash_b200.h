@@ -148,30 +148,6 @@ int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page, int32_t d
                          int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o,
                          int32_t n_seqs, int32_t flags, const int32_t *order, void *stream);
 
-/* The decode of kush_sm100_decode with a stream partition of the work instead of split-KV: for each kv head the
- * pages of the sequences (a sequence's full pages, then its tail page when it has one) laid end to end are cut into
- * n_ctas / hkv equal ranges, one CTA each, so every CTA reads the same number of pages however ragged seq_lens is
- * (n_ctas must be a multiple of hkv; the CTAs of all kv heads with the same range read the same blocks together).
- * A (sequence, kv head) inside one range is written to out by its CTA; the pieces of one cut across ranges go to
- * partials in `work` and a combine merges them (split-KV's merge).  Three launches on `stream` (a one-CTA prefix sum of the sequences' page
- * counts, the decode, the combine); no host synchronisation.  work: fp32, at least kush_sm100_decode_stream_work
- * elements, 16-byte aligned.  Tensor-core configurations only (KUSH_ERR_UNSUPPORTED otherwise).  Outputs agree with
- * kush_sm100_decode within fp32 reassociation of the merge.  No counterpart in the reference (an extension over
- * kushkash/_ops.py:191-213's decode). */
-int kush_sm100_decode_stream(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group, const void *q,
-                             void *out, const void *cache, int64_t block_stride, int64_t head_stride,
-                             const void *tail_k, const int32_t *tail_idx, const int32_t *block_table,
-                             const int32_t *seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_ctas,
-                             float *work, int64_t work_elems, int32_t n_seqs, void *stream);
-
-/* fp32 elements of kush_sm100_decode_stream's work buffer: (n_seqs hkv + n_ctas) group (head_dim + 2) partials plus
- * n_seqs + 1 + n_ctas int32 of partition; 0 on a bad argument. */
-int64_t kush_sm100_decode_stream_work(int32_t n_seqs, int32_t hkv, int32_t group, int32_t head_dim, int32_t n_ctas);
-
-/* The CTAs one wave of the stream decode holds on the current device (resident CTAs per SM x SMs): the natural
- * n_ctas for a large batch.  KUSH_ERR_UNSUPPORTED for a configuration without the tensor-core decode. */
-int kush_sm100_decode_stream_ctas(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);
-
 /* Which decode kernel a configuration takes: 1 = tensor-core kernel (mma), 0 = CUDA-core kernel,
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);

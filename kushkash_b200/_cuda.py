@@ -41,10 +41,6 @@ SIGNATURES = {
     "kush_sm100_decode_ex": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32,
                              _i32, _p, _p, _i32, _i32, _p, _p],
     "kush_sm100_order_longest_first": [_p, _i32, _i32, _p, _p],
-    "kush_sm100_decode_stream": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32,
-                                 _i32, _p, _i64, _i32, _p],
-    "kush_sm100_decode_stream_work": [_i32, _i32, _i32, _i32, _i32],
-    "kush_sm100_decode_stream_ctas": [_i32, _i32, _i32, _i32, _i32],
     "kush_sm100_decode_noalloc": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,
                                   _f32, _i32, _i32, _p],
     "kush_sm100_decode_tensor_cores": [_i32, _i32, _i32, _i32, _i32],
@@ -78,7 +74,6 @@ def lib() -> ctypes.CDLL:
         fn.argtypes = args
         fn.restype = ctypes.c_int32
     dll.kush_sm100_record_bytes.restype = ctypes.c_int64
-    dll.kush_sm100_decode_stream_work.restype = ctypes.c_int64
     dll.kush_sm100_last_error.restype = ctypes.c_char_p
     dll.kush_sm100_version.restype = ctypes.c_char_p
     return dll
@@ -203,13 +198,6 @@ class Kernel:
                        seq_lens, max_pages, hkv, scale, n_splits, part_ml or None, part_o or None, grid[0], flags,
                        order or None, raw_stream(self.device))
 
-    # the decode's arguments up to scale, then the stream partition's CTA count and work buffer
-    def _decode_stream(self, grid, q, out, cache, bs, hs, tail_k, tail_idx, bt, seq_lens, max_pages, hkv, scale, n_ctas,
-                       work, work_elems):
-        c = self.cfg
-        return self.fn(c.head_dim, c.bits, c.page, c.dtype_code, c.group, q, out, cache, bs, hs, tail_k, tail_idx, bt,
-                       seq_lens, max_pages, hkv, scale, n_ctas, work, work_elems, grid[0], raw_stream(self.device))
-
     def _order_longest_first(self, grid, seq_lens, n_seqs, order):
         return self.fn(seq_lens, n_seqs, self.cfg.page, order, raw_stream(self.device))
 
@@ -234,7 +222,7 @@ class Kernel:
 
 
 NAMES = ("append", "write", "decode", "combine", "fwht", "unpack", "append_rotated", "decode_rotated", "combine_rotated",
-         "decode_ex", "order_longest_first", "decode_stream")
+         "decode_ex", "order_longest_first")
 
 
 @lru_cache(None)

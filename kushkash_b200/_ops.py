@@ -26,7 +26,6 @@ _TORCH_DTYPES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.flo
 MAX_SPLITS = 256
 MIN_SPLIT_PAGES = 16
 LONG_SPLIT_PAGES = 100
-MIN_STREAM_PAGES = 16
 
 
 def record_bytes(head_dim: int, bits: int, page: int = PAGE) -> int:
@@ -187,42 +186,6 @@ class Ops:
         if n_splits > 1:
             self.k["combine_rotated" if rotate else "combine"]((S, H, 1), 256, out.data_ptr(), part_ml, part_o,
                                                                n_splits, H)
-
-    def stream_ctas(self, num_seqs: int, num_kv_heads: int, max_full_pages: int) -> int:
-        """CTAs for decode_stream, a multiple of num_kv_heads: one wave of the stream decode kernel on this device,
-        fewer when the batch holds under MIN_STREAM_PAGES pages per CTA (counting num_seqs x (max_full_pages + 1)
-        pages per kv head, an upper bound).  No counterpart in the reference."""
-        if getattr(self, "_wave", None) is None:
-            from . import _cuda
-            c = self.cfg
-            with torch.cuda.device(self.dev):
-                wave = _cuda.lib().kush_sm100_decode_stream_ctas(c.head_dim, c.bits, c.page, c.dtype_code, c.group)
-            if wave <= 0:
-                _cuda.check(wave, "kush_sm100_decode_stream_ctas")
-            self._wave = wave
-        ranges = min(self._wave // num_kv_heads, -(-num_seqs * (max_full_pages + 1) // MIN_STREAM_PAGES))
-        return max(1, ranges) * num_kv_heads
-
-    def stream_work_size(self, num_seqs: int, num_kv_heads: int, n_ctas: int) -> int:
-        """fp32 elements of decode_stream's work buffer: (S * Hkv + n_ctas) * G * (D + 2) partials and S + 1 + n_ctas
-        int32 of partition (kush_sm100_decode_stream_work)."""
-        return (num_seqs * num_kv_heads + n_ctas) * self.G * (self.D + 2) + num_seqs + 1 + n_ctas
-
-    def decode_stream(self, q: torch.Tensor, out: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
-                      seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float, n_ctas: int,
-                      work: torch.Tensor) -> None:
-        """decode() with the stream partition in place of split-KV (an extension): each kv head's pages of all
-        sequences cut into n_ctas / Hkv equal ranges (n_ctas a multiple of Hkv), so a ragged batch loads every CTA
-        alike (stream_ctas() picks n_ctas).  Same outputs as decode() up to fp32 reassociation of the merge.  work: contiguous fp32 of at least
-        stream_work_size(S, Hkv, n_ctas) elements.  Tensor-core configurations only (ValueError otherwise)."""
-        S, H = q.shape[0], tail_k.shape[1]
-        need = self.stream_work_size(S, H, n_ctas)
-        if work.dtype != torch.float32 or not work.is_contiguous() or work.numel() < need:
-            raise ValueError(f"decode_stream: needs a contiguous fp32 work buffer of >= {need} elements")
-        bs, hs = _byte_strides(cache)
-        self.k["decode_stream"]((S, H, 1), 32 * self.cfg.warps, q.data_ptr(), out.data_ptr(), cache.data_ptr(), bs,
-                                hs, tail_k.data_ptr(), tail_idx.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(),
-                                block_table.stride(0), H, float(scale), int(n_ctas), work.data_ptr(), work.numel())
 
     def decode_partials(self, q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                         seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float,

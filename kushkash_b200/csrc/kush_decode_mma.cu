@@ -317,25 +317,15 @@ struct MmaCfg {
 constexpr float TAU = 4.0f;
 
 // grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store;
-// ORD: CTA x works on sequence order[x] (separate instantiations, so the plain kernels keep their code).
-// STR (stream partition): grid (Hkv R); for each kv head, the positions of its units (sequence s with tokens:
-// `setup` positions standing for the fixed cost of a segment, its full pages, then one more for its tail page when it
-// has one) laid end to end in sequence order and cut into R equal ranges, CTA
-// h R + r taking range r of head h one sequence segment at a time (the body below runs once per segment; without
-// STR once).  The CTAs of all kv heads with the same r read the same blocks at the same time, as split-KV's do.
-// spre = [pre[0..S] | start[0..R)]: pre the exclusive prefix sums of the sequences' page counts, start[r] the
-// sequence holding range r's first page (stream_prep_kernel).  A unit wholly inside one range is written to out; the
-// segment of (s, h) in range r is partial h (S + R) + s + r (a unit's partials are contiguous: the ranges after r
-// start at later sequences), merged by combine_stream_kernel.
-template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD, bool STR = false>
+// ORD: CTA x works on sequence order[x] (separate instantiations, so the plain kernels keep their code)
+template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD>
 __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB)) decode_mma_kernel(
     const IN* __restrict__ q, IN* __restrict__ out, const uint8_t* __restrict__ cache, int64_t block_stride,
     int64_t head_stride, const IN* __restrict__ tail_k, const int32_t* __restrict__ tail_idx,
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
     float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o,
     const __grid_constant__ CUtensorMap tmap, int use_tma, uint32_t swz_m, int32_t rows_per_head, int32_t box_rows,
-    const int32_t* __restrict__ order, const int32_t* __restrict__ spre, int n_seqs, int setup) {
-    static_assert(!(STR && (ROT || ORD)), "the stream partition runs unrotated in its own order");
+    const int32_t* __restrict__ order) {
     using F = Fmt<D, BITS, P>;
     using L = Lay<D, BITS>;
     using C = MmaCfg<D, BITS, P, NT>;
@@ -348,56 +338,12 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     float* qsm = reinterpret_cast<float*>(ring + C::RING);              // [G][D] q * scale * log2e
     float* kbr = qsm + G * D;                                           // [D] kb_ref
     __half* kb16 = reinterpret_cast<__half*>(kbr + D);                  // [D] kb_ref as fp16 (read in K pair order)
+    const int s = ORD ? order[blockIdx.x] : blockIdx.x, h = blockIdx.y, z = blockIdx.z;     // launch order
     const int wid = threadIdx.x / WARP, lane = threadIdx.x % WARP, g = lane >> 2, tid = lane & 3;
-    // STR: this CTA's kv head hs and range rr (of nr per head), its pages [f, fend) of the head's pages, the
-    // sequence sq holding page f, the parity of each of this warp's ring slots (kept across segments), and whether a
-    // copy ever failed to complete
-    int64_t f = 0, fend = 0, ppc = 1;
-    int sq = 0, hs = 0, rr = 0, nr = 1;
-    uint32_t phase = 0;
-    bool dead = false;
-    if constexpr (STR) {
-        nr = int(gridDim.x) / H;
-        hs = int(blockIdx.x) / nr;
-        rr = int(blockIdx.x) % nr;
-        const int64_t Th = spre[n_seqs];
-        ppc = (Th + nr - 1) / nr;
-        f = int64_t(rr) * ppc;
-        fend = min(Th, f + ppc);
-        sq = f < Th ? spre[n_seqs + 1 + rr] : 0;
-        if (threadIdx.x == 0) {
-            for (int i = 0; i < NW * NS; i++) mbar_init(&bars[i], 1);
-            fence_mbar_init();                        // (published by the first segment's barrier)
-        }
-    }
-#pragma unroll 1
-    while (true) {
-    int s, h, z;
-    int64_t n, seg0 = 0, seg1 = 0;                    // STR: the segment's pages [seg0, seg1) of its unit
-    bool whole = false;                               // STR: the unit lies in this range alone
-    if constexpr (STR) {
-        if (f >= fend) return;
-        while (spre[sq + 1] <= f) sq++;               // (sequences without tokens hold no pages)
-        const int64_t us = spre[sq], ln = spre[sq + 1] - us;   // the unit's first page and its pages
-        s = sq;
-        h = hs;
-        z = 0;
-        seg0 = f - us;
-        seg1 = min(ln, seg0 + (fend - f));
-        whole = us / ppc == (us + ln - 1) / ppc;
-        f += seg1 - seg0;
-        seg0 = max(seg0 - setup, int64_t(0));          // positions -> pages (a sequence's first `setup` positions
-        seg1 = max(seg1 - setup, int64_t(0));          // stand for its setup cost and hold no page)
-    } else {
-        s = ORD ? order[blockIdx.x] : blockIdx.x;     // launch order
-        h = blockIdx.y;
-        z = blockIdx.z;
-    }
-    n = seq_lens[s];
+    const int64_t n = seq_lens[s];
     const int tail_n = int(n % P);
     const int64_t full = n / P;
-    const SplitRange sr = STR ? SplitRange{seg0, min(seg1, full), true, seg1 > full}
-                              : split_range(seq_lens, int(gridDim.x), s, z, n_splits, P);
+    const SplitRange sr = split_range(seq_lens, int(gridDim.x), s, z, n_splits, P);
     if (!sr.active) {                                                   // no pages here: an empty partial
         for (int hd = threadIdx.x; hd < G; hd += NW * WARP) {
             const int64_t pb = ((int64_t(s) * H + h) * n_splits + z) * G + hd;
@@ -411,13 +357,13 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     const int64_t qbase = (int64_t(s) * H + h) * G * D;
     const uint8_t* hcache = cache + int64_t(h) * head_stride;
 
-    if (!STR && threadIdx.x == 0) {
+    if (threadIdx.x == 0) {
         for (int i = 0; i < NW * NS; i++) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
     // my pages: p0 + wid + i * NW, i < npw; start their copies before anything else
     const int64_t mine0 = p0 + wid;
-    const int npw = !(STR && dead) && mine0 < p1 ? int((p1 - mine0 + NW - 1) / NW) : 0;
+    const int npw = mine0 < p1 ? int((p1 - mine0 + NW - 1) / NW) : 0;
     uint8_t* wcodes = ring + wid * NS * C::CSTRIDE;                     // this warp's code (int4: record) slots
     uint8_t* wscl = ring + NW * NS * C::CODES + wid * NS * C::SCALES;   // and its scale slots (int8)
     uint64_t* wbar = bars + wid * NS;
@@ -505,18 +451,17 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             l[nt][e] = 0.0f;
             vbacc[nt][e] = 0.0f;
         }
-    bool ok = !(STR && dead);
+    bool ok = true;
     int fail_at = npw;
 
 #pragma unroll 1
     for (int i = 0; i < npw; i++) {
         const int slot = int(uint32_t(i) % NS);
-        if (!mbar_wait_u32(bar_u + 8 * slot, STR ? (phase >> slot) & 1u : (uint32_t(i) / NS) & 1u)) {
+        if (!mbar_wait_u32(bar_u + 8 * slot, (uint32_t(i) / NS) & 1u)) {
             ok = false;
             fail_at = i;
             break;
         }
-        if constexpr (STR) phase ^= 1u << slot;
         const uint8_t* codes = wcodes + slot * C::CSTRIDE;               // K rows, then V rows (int8: swizzled)
         const uint8_t* scl = C::SPLIT ? wscl + slot * C::SCALES : codes + C::CODES;   // ks, kb, vs, vb
         // one 16-token tile at a time (P = 32 pages have two): QK, online softmax, PV.  The softmax is tile-granular,
@@ -640,8 +585,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
         // a copy never completed: record it, wait (bounded) for this warp's copies still in flight, produce NaN
         if (lane == 0) atomicExch(&g_decode_error, 1);
         for (int i = fail_at + 1; i < fail_at + NS && i < npw; i++)
-            mbar_wait_u32(bar_u + 8 * (uint32_t(i) % NS),
-                          STR ? (phase >> (uint32_t(i) % NS)) & 1u : (uint32_t(i) / NS) & 1u);
+            mbar_wait_u32(bar_u + 8 * (uint32_t(i) % NS), (uint32_t(i) / NS) & 1u);
     }
     ok = __syncthreads_and(ok);
 
@@ -775,22 +719,16 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             }
         }
         if (!ok) acc = NAN;
-        if (STR ? whole : n_splits == 1) {
+        if (n_splits == 1) {
             out[qbase + idx] = from_f32<IN>(Ls > 0.0f ? acc / Ls : (ok ? 0.0f : NAN));
         } else {
-            const int64_t pb =
-                (STR ? int64_t(h) * (n_seqs + nr) + s + rr : (int64_t(s) * H + h) * n_splits + z) * G + hd;
+            const int64_t pb = ((int64_t(s) * H + h) * n_splits + z) * G + hd;
             part_o[pb * D + d] = acc;
             if (d == 0) {
                 part_ml[pb * 2] = M * 0.69314718055994531f;           // log2 units -> natural, for the combine
                 part_ml[pb * 2 + 1] = Ls;
             }
         }
-    }
-    if constexpr (!STR) return;
-    dead = dead || !ok;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the ring is next filled by tensor copies
-    __syncthreads();
     }
 }
 
@@ -838,14 +776,13 @@ bool make_page_map(const void* cache, int64_t block_stride, int64_t head_stride,
     return true;
 }
 
-template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD, bool STR = false>
+template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD>
 int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                    const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                    int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
-                   int32_t n_seqs, const int32_t* order, cudaStream_t stream, const int32_t* spre = nullptr,
-                   int32_t n_ctas = 0, int32_t setup = 0) {
+                   int32_t n_seqs, const int32_t* order, cudaStream_t stream) {
     using C = MmaCfg<D, BITS, P, NT>;
-    auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT, ORD, STR>;
+    auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT, ORD>;
     CUtensorMap map;
     memset(&map, 0, sizeof(map));
     uint32_t swz_m = 0;
@@ -861,11 +798,11 @@ int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t b
         if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "decode: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         attr_set |= 1ull << (dev & 63);
     }
-    const dim3 grid = STR ? dim3(unsigned(n_ctas)) : dim3(n_seqs, hkv, n_splits);
+    dim3 grid(n_seqs, hkv, n_splits);
     launch_pdl(kern, grid, dim3(MMA_NW * WARP), C::SMEM, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
                static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
                block_table, seq_lens, max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml, part_o, map,
-               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order, spre, n_seqs, setup);
+               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
@@ -885,137 +822,6 @@ int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block
     return launch_mma_rot<D, BITS, P, NT, IN, false, false>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                             tail_idx, block_table, seq_lens, max_pages, hkv, scale,
                                                             n_splits, part_ml, part_o, n_seqs, nullptr, stream);
-}
-
-// ------------------------------------------------------------------ stream partition: prep and combine
-// positions charged to each sequence for the fixed cost of a segment (q, kb_ref, pipeline fill, merge, tail)
-constexpr int STREAM_SETUP_PAGES = 32;
-
-// one CTA of 1024 threads: spre = [pre[0..S] | start[0..R)] for decode_mma_kernel<..., STR>: pre[s] the positions of
-// the sequences before s (a sequence with tokens: `setup`, its full pages, one for a partial tail page), start[r] the
-// last sequence s with
-// pre[s] <= r ppc (the sequence holding range r's first page; 0 for an empty range), ppc = ceil(pre[S] / R)
-__global__ void __launch_bounds__(1024) stream_prep_kernel(const int32_t* __restrict__ seq_lens, int n_seqs, int P,
-                                                           int n_ranges, int setup, int32_t* __restrict__ spre) {
-    __shared__ int32_t wsum[32];
-    __shared__ int32_t carry;
-    pdl_wait();                                       // previous kernel on the stream done (it may append tokens)
-    const int t = threadIdx.x, lane = t % WARP, w = t / WARP;
-    if (t == 0) {
-        carry = 0;
-        spre[0] = 0;
-    }
-    __syncthreads();
-    for (int b = 0; b < n_seqs; b += 1024) {          // block scan, 1024 sequences at a time
-        const int s = b + t;
-        int v = 0;
-        if (s < n_seqs) {
-            const int n = seq_lens[s];
-            v = n > 0 ? setup + n / P + (n % P != 0 ? 1 : 0) : 0;
-        }
-#pragma unroll
-        for (int o = 1; o < WARP; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, v, o);
-            if (lane >= o) v += y;
-        }
-        if (lane == WARP - 1) wsum[w] = v;
-        __syncthreads();
-        if (w == 0) {
-            int x = wsum[lane];
-#pragma unroll
-            for (int o = 1; o < WARP; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, x, o);
-                if (lane >= o) x += y;
-            }
-            wsum[lane] = x;
-        }
-        __syncthreads();
-        const int incl = carry + (w ? wsum[w - 1] : 0) + v;
-        if (s < n_seqs) spre[s + 1] = incl;
-        __syncthreads();
-        if (t == 1023) carry = incl;
-        __syncthreads();
-    }
-    const int64_t T = carry, ppc = (T + n_ranges - 1) / n_ranges;
-    for (int r = t; r < n_ranges; r += 1024) {
-        const int64_t f = int64_t(r) * ppc;
-        int lo = 0;
-        if (f < T) {
-            int hi = n_seqs - 1;
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) / 2;
-                if (spre[mid] <= f)
-                    lo = mid;
-                else
-                    hi = mid - 1;
-            }
-        }
-        spre[n_seqs + 1 + r] = lo;
-    }
-}
-
-// grid (S Hkv G), block D: the output of (sequence s, kv head h, group head g) from its partials h (S + R) + s + r,
-// r = r0..r1 (the ranges its pages span); a unit inside one range was written by the decode, one without pages gets
-// zeros
-template <class IN>
-__global__ void __launch_bounds__(256) combine_stream_kernel(IN* __restrict__ out, const float* __restrict__ part_ml,
-                                                             const float* __restrict__ part_o,
-                                                             const int32_t* __restrict__ spre, int n_seqs, int H, int G,
-                                                             int D, int n_ctas) {
-    pdl_wait();                                       // the decode done
-    const int64_t u = blockIdx.x / G, g = blockIdx.x % G;
-    const int s = int(u / H), h = int(u % H), d = threadIdx.x;
-    const int64_t ln = spre[s + 1] - spre[s];
-    IN* o = out + (u * G + g) * D + d;
-    if (ln == 0) {
-        *o = from_f32<IN>(0.0f);
-        return;
-    }
-    const int nr = n_ctas / H;
-    const int64_t ppc = (int64_t(spre[n_seqs]) + nr - 1) / nr;
-    const int64_t us = spre[s], c0 = us / ppc, c1 = (us + ln - 1) / ppc;
-    if (c0 == c1) return;
-    const int64_t first = int64_t(h) * (n_seqs + nr) + s + c0;
-    *o = from_f32<IN>(merge_splits(part_ml + (first * G + g) * 2, part_o + (first * G + g) * D + d, int(c1 - c0 + 1),
-                                   G, D));
-}
-
-// resident CTAs per SM of the stream decode kernel (what one wave of it holds)
-template <int D, int BITS, int P, int NT, class IN>
-int stream_resident_per_sm(int* per_sm) {
-    using C = MmaCfg<D, BITS, P, NT>;
-    auto kern = decode_mma_kernel<D, BITS, P, NT, IN, false, false, true>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, MMA_NW * WARP, C::SMEM);
-    if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "decode_stream: occupancy query: %s", cudaGetErrorString(e));
-    return KUSH_OK;
-}
-
-// the stream decode (per_sm null) or its occupancy query
-int decode_stream_mma(int D, int bits, int P, int dtype, int G, const void* q, void* out, const void* cache,
-                      int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
-                      const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
-                      float* part_ml, float* part_o, const int32_t* spre, int32_t n_ctas, int32_t n_seqs, int* per_sm,
-                      cudaStream_t stream) {
-    auto go = [&](auto Dc, auto Bc, auto Pc, auto in) -> int {
-        using IN = decltype(in);
-        auto run = [&](auto ntc) -> int {
-            constexpr int NT = decltype(ntc)::value;
-            if (per_sm) return stream_resident_per_sm<Dc.value, Bc.value, Pc.value, NT, IN>(per_sm);
-            return launch_mma_rot<Dc.value, Bc.value, Pc.value, NT, IN, false, false, true>(
-                G, q, out, cache, block_stride, head_stride, tail_k, tail_idx, block_table, seq_lens, max_pages, hkv,
-                scale, 1, part_ml, part_o, n_seqs, nullptr, stream, spre, n_ctas, STREAM_SETUP_PAGES);
-        };
-        if constexpr (std::is_same_v<IN, float>) {
-            return KUSH_ERR_UNSUPPORTED;
-        } else if constexpr (Dc.value == 256) {
-            return run(std::integral_constant<int, 1>{});
-        } else {
-            if (G <= 8) return run(std::integral_constant<int, 1>{});
-            return run(std::integral_constant<int, 2>{});
-        }
-    };
-    return dispatch_fmt(D, bits, P, dtype, go);
 }
 
 int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
@@ -1052,74 +858,6 @@ int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, v
 }
 
 }  // namespace kush
-
-using namespace kush;
-
-extern "C" int64_t kush_sm100_decode_stream_work(int32_t n_seqs, int32_t hkv, int32_t group, int32_t head_dim,
-                                                 int32_t n_ctas) {
-    if (n_seqs < 0 || hkv < 1 || group < 1 || head_dim < 1 || n_ctas < 1) return 0;
-    return (int64_t(n_seqs) * hkv + n_ctas) * group * (head_dim + 2) + n_seqs + 1 + n_ctas;
-}
-
-extern "C" int kush_sm100_decode_stream_ctas(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype,
-                                             int32_t group) {
-    if (kush_sm100_record_bytes(head_dim, bits, page) == 0 || !decode_mma_supported(head_dim, bits, page, dtype, group))
-        return set_error(KUSH_ERR_UNSUPPORTED, "kush_sm100_decode_stream_ctas: head_dim %d bits %d page %d dtype %d "
-                                               "group %d has no tensor-core decode", head_dim, bits, page, dtype, group);
-    int per_sm = 0, dev = 0, sms = 0;
-    int rc = decode_stream_mma(head_dim, bits, page, dtype, group, nullptr, nullptr, nullptr, 0, 0, nullptr, nullptr,
-                               nullptr, nullptr, 0, 1, 1.0f, nullptr, nullptr, nullptr, 1, 1, &per_sm, nullptr);
-    if (rc != KUSH_OK) return rc;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return set_error(KUSH_ERR_CUDA, "kush_sm100_decode_stream_ctas: %s", cudaGetErrorString(e));
-    return per_sm * sms;
-}
-
-extern "C" int kush_sm100_decode_stream(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
-                                        const void* q, void* out, const void* cache, int64_t block_stride,
-                                        int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
-                                        const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages,
-                                        int32_t hkv, float scale, int32_t n_ctas, float* work, int64_t work_elems,
-                                        int32_t n_seqs, void* stream) {
-    if (n_seqs < 0 || hkv < 1 || group < 1 || n_ctas < 1 || n_ctas > (1 << 30) || n_ctas % hkv)
-        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_stream: n_seqs %d hkv %d group %d n_ctas %d (a multiple of "
-                                       "hkv)", n_seqs, hkv, group, n_ctas);
-    if (n_seqs == 0) return KUSH_OK;
-    if (kush_sm100_record_bytes(head_dim, bits, page) == 0 || !decode_mma_supported(head_dim, bits, page, dtype, group))
-        return set_error(KUSH_ERR_UNSUPPORTED, "kush_sm100_decode_stream: head_dim %d bits %d page %d dtype %d group "
-                                               "%d has no tensor-core decode", head_dim, bits, page, dtype, group);
-    if (!q || !out || !cache || !tail_k || !tail_idx || !block_table || !seq_lens || !work)
-        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_stream: null pointer");
-    const int64_t need = kush_sm100_decode_stream_work(n_seqs, hkv, group, head_dim, n_ctas);
-    if (work_elems < need)
-        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_stream: work holds %lld fp32 elements, needs %lld",
-                         (long long)work_elems, (long long)need);
-    if (!aligned16(cache) || (block_stride & 15) || (head_stride & 15) || !aligned16(tail_k) || !aligned16(q) ||
-        !aligned16(out))
-        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_stream: records, q, out and tail_k must be 16-byte aligned");
-    const int64_t parts = (int64_t(n_seqs) * hkv + n_ctas) * group;
-    float* part_ml = work;
-    float* part_o = work + parts * 2;
-    int32_t* spre = reinterpret_cast<int32_t*>(part_o + parts * head_dim);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    launch_pdl(stream_prep_kernel, dim3(1), dim3(1024), 0, st, seq_lens, n_seqs, int(page), int(n_ctas / hkv),
-               int(STREAM_SETUP_PAGES), spre);
-    int rc = check_launch("kush_sm100_decode_stream (prep)");
-    if (rc != KUSH_OK) return rc;
-    rc = decode_stream_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
-                           tail_idx, block_table, seq_lens, max_pages, hkv, scale, part_ml, part_o, spre, n_ctas, n_seqs,
-                           nullptr, st);
-    if (rc != KUSH_OK) return rc;
-    rc = dispatch_dtype(dtype, [&](auto in) {
-        using IN = decltype(in);
-        launch_pdl(combine_stream_kernel<IN>, dim3(unsigned(int64_t(n_seqs) * hkv * group)), dim3(head_dim), 0, st,
-                   static_cast<IN*>(out), static_cast<const float*>(part_ml), static_cast<const float*>(part_o),
-                   static_cast<const int32_t*>(spre), int(n_seqs), int(hkv), int(group), int(head_dim), int(n_ctas));
-        return check_launch("kush_sm100_decode_stream (combine)");
-    });
-    return rc;
-}
 
 extern "C" int kush_sm100_device_error(int32_t clear) {
     int v = 0;

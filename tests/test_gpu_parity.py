@@ -179,82 +179,6 @@ def test_decode_ragged_splits(n_splits, dtype):
     assert_close(out, want, dtype, f"ragged splits={n_splits}")
 
 
-def ragged_state(D, bits, G, P, H, lens, seed, dtype=torch.bfloat16, oracle=True):
-    """A ragged batch written by the bulk write on the GPU (and by the oracle when `oracle`): (gpu ops, gpu state,
-    oracle ops, oracle state, q on the CPU)."""
-    B = len(lens)
-    pages = max(1, max(-(-n // P) for n in lens))
-    g = torch.Generator().manual_seed(seed)
-    bt = torch.randperm(B * pages, generator=g).to(torch.int32).view(B, pages)
-    T = sum(lens)
-    k = exact(torch.randn(T, H, D, generator=g) + 3 * torch.randn(H, D, generator=g), dtype)
-    v = exact(torch.randn(T, H, D, generator=g), dtype)
-    q = exact(torch.randn(B, H * G, D, generator=g), dtype)
-    qsl = torch.tensor([0] + lens, dtype=torch.int64).cumsum(0).to(torch.int32)
-    npg = [-(-n // P) for n in lens]
-    js = torch.tensor([s for s in range(B) for _ in range(npg[s])], dtype=torch.int32)
-    jp = torch.tensor([p for s in range(B) for p in range(npg[s])], dtype=torch.int32)
-    sl = torch.tensor(lens, dtype=torch.int32)
-    go = gpu_ops(D, bits, G, dtype, P)
-    st = make_state(B, H, D, bits, P, bt, B * pages, "cuda", dtype)
-    st.seq_lens.copy_(sl.cuda())
-    go.write(k.to("cuda", dtype), v.to("cuda", dtype), qsl.cuda(), st.seq_lens, st.tail_idx, js.cuda(), jp.cuda(),
-             st.pool, st.block_table, st.tail_k)
-    ro = ref = None
-    if oracle:
-        ro = OracleOps(D, bits, G, P)
-        ref = make_state(B, H, D, bits, P, bt, B * pages)
-        ref.seq_lens.copy_(sl)
-        ro.write(k, v, qsl, ref.seq_lens, ref.tail_idx, js, jp, ref.pool, ref.block_table, ref.tail_k)
-        assert torch.equal(st.pool.cpu(), ref.pool)
-    return go, st, ro, ref, q
-
-
-STREAM_GEOMETRIES = [(128, 8, 7, 32, 4), (128, 4, 4, 16, 2), (128, 4, 4, 32, 2), (64, 4, 8, 16, 2), (256, 8, 2, 16, 1),
-                     (128, 4, 16, 16, 1)]
-
-
-@pytest.mark.parametrize("D,bits,G,P,H", STREAM_GEOMETRIES)
-@pytest.mark.parametrize("ranges", [1, 5, 37, 0])
-def test_decode_stream(D, bits, G, P, H, ranges):
-    """The stream partition on a ragged batch (0 tokens .. 200 pages, tail-only, page-aligned) gives the oracle's
-    outputs at every range count per kv head: one range (every sequence a segment of one CTA, written directly), a
-    few ranges (sequences cut across CTAs, merged by the combine), and stream_ctas() (0 here); the work buffer and
-    outputs start as NaN, so a partial or output left unwritten fails."""
-    from kushkash_b200._cuda import device_error
-    lens = [0, 1, 9, P, 3 * P + 5, 40 * P + 7, 200 * P, 17 * P + 15, 64 * P + 1]
-    go, st, ro, ref, q = ragged_state(D, bits, G, P, H, lens, 31)
-    B = len(lens)
-    want = torch.empty(B, H * G, D)
-    ro.decode(q.contiguous(), want, ref.pool, ref.block_table, ref.seq_lens, ref.tail_idx, ref.tail_k, D ** -0.5)
-    C = ranges * H or go.stream_ctas(B, H, max(lens) // P)
-    out = torch.full((B, H * G, D), float("nan"), dtype=torch.bfloat16, device="cuda")
-    work = torch.full((go.stream_work_size(B, H, C),), float("nan"), device="cuda")
-    go.decode_stream(q.to("cuda", torch.bfloat16).contiguous(), out, st.pool, st.block_table, st.seq_lens, st.tail_idx,
-                     st.tail_k, D ** -0.5, C, work)
-    assert_close(out, want, torch.bfloat16, f"stream C={C}")
-    assert device_error(clear=True) == 0
-
-
-def test_decode_stream_many_sequences():
-    """1500 short sequences (0 .. 3 pages: the prefix sum runs over two 1024-sequence blocks) and one long one, at a
-    wave of CTAs and at 3 ranges per kv head: the stream decode agrees with the split-KV decode (itself held to the oracle above) within
-    the merge's fp32 reassociation."""
-    D, bits, G, P, H = 128, 4, 4, 16, 2
-    g = torch.Generator().manual_seed(41)
-    lens = torch.randint(0, 3 * P + 1, (1500,), generator=g).tolist() + [300 * P + 3]
-    go, st, _, _, q = ragged_state(D, bits, G, P, H, lens, 43, oracle=False)
-    B = len(lens)
-    qd = q.to("cuda", torch.bfloat16).contiguous()
-    want = torch.empty(B, H * G, D, dtype=torch.bfloat16, device="cuda")
-    go.decode(qd, want, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5)
-    for C in (go.stream_ctas(B, H, max(lens) // P), 3 * H):
-        out = torch.full_like(want, float("nan"))
-        work = torch.full((go.stream_work_size(B, H, C),), float("nan"), device="cuda")
-        go.decode_stream(qd, out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5, C, work)
-        assert_close(out, want, torch.bfloat16, f"stream many C={C}")
-
-
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("n_splits", [1, 3])
 def test_decode_longest_first_order(n_splits, dtype):

@@ -28,16 +28,6 @@ def test_library_exports_every_declared_symbol():
     assert lib().kush_sm100_version().startswith(b"kushkash_b200")
 
 
-def test_stream_work_size_agrees():
-    """The stream decode's work size (C-ABI host arithmetic) is the layout Ops.stream_work_size allocates:
-    (S Hkv + C) G (D + 2) partials plus S + 1 + C int32 of partition; 0 on a bad argument."""
-    from kushkash_b200._cuda import lib
-    for S, H, G, D, C in [(1, 1, 1, 64, 1), (64, 4, 7, 128, 444), (2048, 8, 4, 128, 592), (3, 2, 16, 256, 7)]:
-        assert lib().kush_sm100_decode_stream_work(S, H, G, D, C) == (S * H + C) * G * (D + 2) + S + 1 + C
-    assert lib().kush_sm100_decode_stream_work(1, 0, 1, 64, 1) == 0
-    assert lib().kush_sm100_decode_stream_work(1, 1, 1, 64, 0) == 0
-
-
 def test_record_bytes_agree():
     from kushkash_b200._cuda import lib
     from kushkash_b200 import record_bytes
