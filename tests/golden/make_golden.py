@@ -1,7 +1,7 @@
 """Generates tests/golden/golden.npz and golden.json from the REFERENCE's own PyTorch pins.
 
-Run in a container where the reference checkout is importable (it is read from KUSHKASH_REF, default
-/root/reference; nothing at test time reads it):
+Run in a container where the reference checkout is importable (the directory named by KUSHKASH_REF; nothing at
+test time reads it):
 
     python tests/golden/make_golden.py
 
