@@ -226,8 +226,12 @@ NAMES = ("append", "write", "decode", "combine", "fwht", "unpack", "append_rotat
 
 
 @lru_cache(None)
-def kernels(device: int, cfg: GpuConfig) -> dict[str, Kernel]:
-    """{name: Kernel} for one device and configuration (kushkash/_cuda.py:106-108)."""
+def kernels(device: int, cfg) -> dict[str, Kernel]:
+    """{name: Kernel} for one device and configuration (kushkash/_cuda.py:106-108).  `cfg` is this package's
+    GpuConfig or any object with the reference GpuConfig's fields (head_dim, bits, group, dtype, arch; page 32
+    when it has none)."""
+    if not isinstance(cfg, GpuConfig):
+        cfg = GpuConfig(cfg.head_dim, cfg.bits, cfg.group, cfg.dtype, cfg.arch, getattr(cfg, "page", 32))
     return {name: Kernel(device, cfg, name) for name in NAMES}
 
 

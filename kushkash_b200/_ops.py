@@ -1,43 +1,45 @@
-"""Operator surface over the page-record layout: the B200 replacement of the reference's dispatch layer
-(kushkash/_ops.py:42-213, class Ops), with the same method names, arguments and error behaviour.
+"""kushkash_b200.Ops: the library's own PyTorch-facing operator object, one per (device, head_dim, bits, group,
+dtype, page), calling the C ABI of libkush_sm100.so (include/kushkash_b200.h) directly.
 
-Tensor conventions (as kushkash/_ops.py:6-15):
-  cache       any tensor whose dim 0 is the block and dim 1 the kv head, each (block, head) record contiguous:
-              uint8 [pages, H, RB] or [blocks, H, P, RB // P]; byte strides are passed, so it may be a slice
-  tail_k      [slots, H, P, D] in the kernel dtype: K of the page being filled, exact; sequence s uses slot
-              tail_idx[s]; its V rows are already final in the page's record
-  k, v rows   [rows, H, D] (row strides free, may differ between k and v; head stride D)
-  q, out      [S, Hq, D] contiguous (q head = kv_head * G + g)
-  rotation    the kernels do not rotate; callers pass rotated q, k, v (fwht / rotate) and rotate the output back
+Two ways reach the same kernels:
+  * the reference's own operator layer (kushkash/_ops.py Ops, cache.py KushCache, the HF / vLLM / SGLang
+    integrations), unchanged, through the drop-in loader kushkash_b200._cuda (kushkash_b200.dropin.install());
+  * this class, which the benchmarks, the sharding layer and the parity tests use.  Its calls take the same
+    tensors with the same meaning as kushkash.Ops (kushkash/_ops.py:42-213) -- so code written against one reads
+    the same against the other -- plus what the reference cannot express: the page size (16 or 32 tokens), the
+    rotation fused into the kernels, a decode launch order and the split-KV partials without their combine.
 
-Every kernel runs on the CUDA device on torch's current stream.  There is no CPU path and no PyTorch fallback:
-constructing Ops for a non-CUDA device raises, and a missing kernel library raises on first use.
+Tensor conventions (the record layout of kushkash/kush/quant.mojo:53-87):
+  cache        [blocks, H, ...] uint8 (any view whose (block, head) records are contiguous; byte strides are passed)
+  tail_k       [slots, H, P, D] in the kernel dtype: exact K of each sequence's unfinished page (slot tail_idx[s])
+  k, v rows    [rows, H, D], row strides free, head stride D
+  q, out       [S, H * G, D] contiguous, q head = kv_head * G + g
+  index tensors int32 on the device
+
+Every call is asynchronous on torch's current stream of the device; nothing allocates except the optional outputs
+of fwht() and longest_first().  There is no CPU path and no PyTorch fallback: a non-CUDA device, a missing library
+or an unsupported configuration raises.
 """
 from __future__ import annotations
 
-import math
 import os
 
 import torch
 
+from . import _cuda
 from ._build import PAGE, GpuConfig
 
-_TORCH_DTYPES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32"}
+_DTYPE_NAMES = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32"}
 MAX_SPLITS = 256
 MIN_SPLIT_PAGES = 16
 LONG_SPLIT_PAGES = 100
 
 
 def record_bytes(head_dim: int, bits: int, page: int = PAGE) -> int:
-    """Bytes of one (page, kv head) record (kushkash/_ops.py:29-31, kushkash/kush/quant.mojo:60-62)."""
+    """Bytes of one (page, kv head) record: P code rows each for K and V (D bytes at 8 bits, D/2 at 4) and fp16
+    K scale / bias per channel and V scale / bias per token (the format of kushkash/kush/quant.mojo:53-87)."""
     dc = head_dim if bits == 8 else head_dim // 2
     return 2 * page * dc + 4 * head_dim + 4 * page
-
-
-def _byte_strides(cache: torch.Tensor) -> tuple[int, int]:
-    """Block and head strides in bytes (kushkash/_ops.py:34-39)."""
-    e = cache.element_size()
-    return cache.stride(0) * e, cache.stride(1) * e
 
 
 def split_factor(num_seqs: int, num_kv_heads: int, max_full_pages: int, sms: int, ctas_per_sm: int = 4) -> int:
@@ -59,105 +61,118 @@ def split_factor(num_seqs: int, num_kv_heads: int, max_full_pages: int, sms: int
     return ns
 
 
+def _pool(cache: torch.Tensor) -> tuple[int, int, int]:
+    """(address, block stride, head stride) of a record pool, strides in bytes."""
+    e = cache.element_size()
+    return cache.data_ptr(), cache.stride(0) * e, cache.stride(1) * e
+
+
+def _table(block_table: torch.Tensor) -> tuple[int, int]:
+    """(address, row stride in entries) of a block table."""
+    return block_table.data_ptr(), block_table.stride(0)
+
+
+def _need(ok: bool, what: str) -> None:
+    if not ok:
+        raise ValueError(what)
+
+
 class Ops:
-    """Kernels for one (device, head_dim, bits, q-heads-per-kv-head, dtype[, page]) (kushkash/_ops.py:42-63)."""
+    """The kernels of one (device, head_dim, bits, group, dtype, page) configuration."""
 
     def __init__(self, device: torch.device, head_dim: int, bits: int, group: int, dtype: torch.dtype,
                  page: int = PAGE):
         device = torch.device(device)
-        if device.type != "cuda":
-            raise ValueError("kushkash_b200 runs on CUDA (B200, sm_100a) devices only; it has no CPU path")
-        if head_dim not in (64, 128, 256):
-            raise ValueError("GPU head_dim must be 64, 128 or 256")
-        if dtype not in _TORCH_DTYPES:
-            raise ValueError(f"dtype must be one of {tuple(_TORCH_DTYPES)}")
-        from . import _cuda
-        self.device, self.D, self.bits, self.G, self.dtype, self.P = device, head_dim, bits, group, dtype, page
-        self.gpu = True
-        dev = device.index if device.index is not None else torch.cuda.current_device()
-        self.dev = dev
-        self.cfg = GpuConfig(head_dim, bits, group, _TORCH_DTYPES[dtype], _cuda.arch(dev), page)
-        self.k = _cuda.kernels(dev, self.cfg)
-        self.sms = _cuda.sm_count(dev)
+        _need(device.type == "cuda", "kushkash_b200 runs on CUDA (B200, sm_100a) devices only; it has no CPU path")
+        _need(head_dim in (64, 128, 256), "GPU head_dim must be 64, 128 or 256")
+        _need(dtype in _DTYPE_NAMES, f"dtype must be one of {tuple(_DTYPE_NAMES)}")
+        self.dev = device.index if device.index is not None else torch.cuda.current_device()
+        self.device = torch.device("cuda", self.dev)
+        self.D, self.bits, self.G, self.dtype, self.P = head_dim, bits, group, dtype, page
+        self.cfg = GpuConfig(head_dim, bits, group, _DTYPE_NAMES[dtype], _cuda.arch(self.dev), page)
+        self.sms = _cuda.sm_count(self.dev)
+        self.lib = _cuda.lib()
+        self._fmt = (head_dim, bits, page, self.cfg.dtype_code)        # leading arguments of most entry points
         self.fused_write = os.environ.get("KUSHKASH_FUSED_WRITE", "1") != "0"
 
-    # ---------------------------------------------------------------- writes
+    def _run(self, entry: str, *args) -> None:
+        """Call one C entry point with torch's current stream of this device appended; raise on a failed status."""
+        fn = getattr(self.lib, entry)
+        if torch.cuda.current_device() == self.dev:
+            rc = fn(*args, _cuda.raw_stream(self.dev))
+        else:
+            with torch.cuda.device(self.dev):
+                rc = fn(*args, _cuda.raw_stream(self.dev))
+        _cuda.check(rc, entry)
+
+    # ---------------------------------------------------------------- quantize-on-write
     def append(self, k: torch.Tensor, v: torch.Tensor, seq_lens: torch.Tensor, tail_idx: torch.Tensor,
-               cache: torch.Tensor, block_table: torch.Tensor, tail_k: torch.Tensor,
-               pos_offset: int, advance: bool, *, rotate: bool = False) -> None:
-        """One token per sequence: row s of k/v goes to position seq_lens[s] + pos_offset (kushkash/_ops.py:66-80).
-        rotate=True (an extension): the rows are rotated (canonical Walsh-Hadamard) inside the kernel first, bit for
-        bit what fwht() then append() store."""
-        S, H = k.shape[0], k.shape[1]
-        bs, hs = _byte_strides(cache)
-        self.k["append_rotated" if rotate else "append"]((S, 1, 1), self.D, k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), seq_lens.data_ptr(),
-                         pos_offset, int(advance), tail_idx.data_ptr(), cache.data_ptr(), bs, hs,
-                         tail_k.data_ptr(), block_table.data_ptr(), block_table.stride(0), H)
+               cache: torch.Tensor, block_table: torch.Tensor, tail_k: torch.Tensor, pos_offset: int, advance: bool,
+               *, rotate: bool = False) -> None:
+        """One new token per sequence: row s of k / v lands at position seq_lens[s] + pos_offset (negative positions
+        are skipped); advance stores pos + 1 into seq_lens.  rotate: rotate the rows first (canonical Walsh-Hadamard,
+        bit for bit what fwht() then append() store)."""
+        entry = "kush_sm100_append_rotated" if rotate else "kush_sm100_append"
+        self._run(entry, *self._fmt, k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), seq_lens.data_ptr(),
+                  int(pos_offset), int(bool(advance)), tail_idx.data_ptr(), *_pool(cache), tail_k.data_ptr(),
+                  *_table(block_table), k.shape[1], k.shape[0])
 
     def write(self, k: torch.Tensor, v: torch.Tensor, query_start_loc: torch.Tensor, seq_lens: torch.Tensor,
               tail_idx: torch.Tensor, job_seq: torch.Tensor, job_page: torch.Tensor, cache: torch.Tensor,
               block_table: torch.Tensor, tail_k: torch.Tensor) -> None:
-        """Ragged multi-token write (kushkash/_ops.py:82-101).  Sequence s owns rows [qsl[s], qsl[s+1]) at positions
-        ending at seq_lens[s] (already counting them); one job per (sequence, logical page) touched.  One launch
-        (mode 2) unless KUSHKASH_FUSED_WRITE=0, which runs the reference's two launches (mode 0, then mode 1)."""
-        n_jobs, H = job_seq.numel(), k.shape[1]
+        """Ragged multi-token write: sequence s owns rows [qsl[s], qsl[s+1]) at the positions that end at
+        seq_lens[s] (which already counts them); job j is logical page job_page[j] of sequence job_seq[j].  One
+        launch (mode 2); KUSHKASH_FUSED_WRITE=0 (or fused_write = False) runs the two-launch form (modes 0, 1)."""
+        n_jobs = job_seq.numel()
         if n_jobs == 0:
             return
-        bs, hs = _byte_strides(cache)
         for mode in ((2,) if self.fused_write else (0, 1)):
-            self.k["write"]((n_jobs, H, 1), self.D, k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0),
-                            query_start_loc.data_ptr(), seq_lens.data_ptr(), tail_idx.data_ptr(),
-                            job_seq.data_ptr(), job_page.data_ptr(), mode, cache.data_ptr(), bs, hs,
-                            tail_k.data_ptr(), block_table.data_ptr(), block_table.stride(0), H)
+            self._run("kush_sm100_write", *self._fmt, k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0),
+                      query_start_loc.data_ptr(), seq_lens.data_ptr(), tail_idx.data_ptr(), job_seq.data_ptr(),
+                      job_page.data_ptr(), mode, *_pool(cache), tail_k.data_ptr(), *_table(block_table), k.shape[1],
+                      n_jobs)
 
-    # ---------------------------------------------------------------- rotation
+    # ---------------------------------------------------------------- rotation and unpack
     def fwht(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Canonical Walsh-Hadamard rotation of every D-row of contiguous x (kushkash/_ops.py:104-127); out may be x."""
-        D = self.D
-        if x.shape[-1] != D or not x.is_contiguous():
-            raise ValueError(f"fwht: x must be contiguous with last dim {D}")
-        out = torch.empty_like(x) if out is None else out
-        if out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous():
-            raise ValueError("fwht: out must be contiguous, with x's shape and dtype")
-        rows = x.numel() // D
-        if rows == 0:
-            return out
-        if x.dtype != self.dtype:
-            raise ValueError(f"fwht: x is {x.dtype}, these kernels take {self.dtype}")
-        self.k["fwht"](((rows + 3) // 4, 1, 1), 128, x.data_ptr(), out.data_ptr(), D, D, rows)
-        return out
+        """The canonical Walsh-Hadamard rotation of every D-row of x (contiguous, this dtype) into out (a new
+        tensor, or x itself, or any contiguous tensor of x's shape and dtype); returns out."""
+        y = torch.empty_like(x) if out is None else out
+        _need(x.dtype == self.dtype and y.dtype == self.dtype, f"fwht: tensors must be {self.dtype}")
+        _need(x.is_contiguous() and y.is_contiguous() and x.shape == y.shape and x.shape[-1] == self.D,
+              f"fwht: x and out must be contiguous, of one shape, with last dim {self.D}")
+        rows = x.numel() // self.D
+        if rows:
+            self._run("kush_sm100_fwht", self.D, self.cfg.dtype_code, x.data_ptr(), y.data_ptr(), self.D, self.D,
+                      rows)
+        return y
 
-    # ---------------------------------------------------------------- unpack (prefill with history)
     def unpack(self, cache: torch.Tensor, page_blk: torch.Tensor, page_dst: torch.Tensor, tail_blk: torch.Tensor,
                tail_info: torch.Tensor, tail_k: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                new_dst: torch.Tensor, kp: torch.Tensor, vp: torch.Tensor, rot: bool) -> None:
-        """One packed-prefill group's keys / values into kp, vp ([rows, Hkv, D], contiguous), one launch
-        (kushkash/_ops.py:129-179); same checks and errors."""
-        H, D = kp.shape[1], self.D
+        """Keys and values of a prefill with history into kp / vp ([rows, H, D], contiguous, this dtype): full pages
+        (block page_blk[i] -> rows page_dst[i] + t), partial pages (block tail_blk[i], tail_info[i] = first row,
+        tokens, tail slot; K from tail_k), new rows (row j of k_new / v_new -> row new_dst[j]); rot rotates history
+        back.  Index values are not checked on the host (that would synchronise); the tensors' kinds are."""
+        H = kp.shape[1]
+        idx = (page_blk, page_dst, tail_blk, tail_info, new_dst)
+        _need(all(t.dtype == torch.int32 and t.is_contiguous() for t in idx), "unpack: index tensors must be "
+              "contiguous int32")
+        _need(all(t.dtype == self.dtype for t in (tail_k, k_new, v_new, kp, vp)),
+              f"unpack: tail_k, k_new, v_new, kp and vp must be {self.dtype}")
+        _need(kp.shape == vp.shape and kp.dim() == 3 and kp.shape[2] == self.D and kp.is_contiguous()
+              and vp.is_contiguous(), f"unpack: kp and vp must be contiguous [rows, H, {self.D}]")
+        _need(all(t.dim() == 3 and tuple(t.shape[1:]) == (H, self.D) and t.stride(1) == self.D and t.stride(2) == 1
+                  for t in (k_new, v_new)), "unpack: k_new / v_new rows must be [n, H, D] with head stride D")
         n_pages, n_tail, n_new = page_blk.numel(), tail_blk.numel(), new_dst.numel()
-        for t in (page_blk, page_dst, tail_blk, tail_info, new_dst):
-            if t.dtype != torch.int32 or not t.is_contiguous():
-                raise ValueError("unpack: index tensors must be contiguous int32")
-        if not (kp.is_contiguous() and vp.is_contiguous() and kp.shape == vp.shape and kp.shape[2] == D):
-            raise ValueError("unpack: kp / vp must be contiguous [rows, Hkv, D]")
-        for t in (k_new, v_new):
-            if t.shape[1:] != (H, D) or t.stride(2) != 1 or t.stride(1) != D:
-                raise ValueError("unpack: k_new / v_new must be [n, Hkv, D] with unit dim stride and head stride D")
-        if tail_info.numel() != 3 * n_tail or k_new.shape[0] < n_new or v_new.shape[0] < n_new:
-            raise ValueError("unpack: tail_info must hold 3 ints per partial page; k_new / v_new one row per new_dst")
-        if page_dst.numel() != n_pages:
-            raise ValueError("unpack: page_dst must hold one row per page_blk entry")
-        for t in (tail_k, k_new, v_new, kp, vp):
-            if t.dtype != self.dtype:
-                raise ValueError(f"unpack: tail_k, k_new, v_new, kp, vp must be {self.dtype}, got {t.dtype}")
+        _need(page_dst.numel() == n_pages and tail_info.numel() == 3 * n_tail
+              and min(k_new.shape[0], v_new.shape[0]) >= n_new,
+              "unpack: one page_dst per page, three tail_info ints per partial page, one k_new / v_new row per new_dst")
         if n_pages + n_tail + n_new == 0:
             return
-        bs, hs = _byte_strides(cache)
-        grid = (n_pages + n_tail + (n_new + 31) // 32, H, 1)
-        self.k["unpack"](grid, 128, cache.data_ptr(), bs, hs, H, page_blk.data_ptr(), page_dst.data_ptr(), n_pages,
-                         tail_blk.data_ptr(), tail_info.data_ptr(), n_tail, tail_k.data_ptr(), k_new.data_ptr(),
-                         v_new.data_ptr(), k_new.stride(0), v_new.stride(0), new_dst.data_ptr(), n_new, kp.data_ptr(),
-                         vp.data_ptr(), int(rot))
+        self._run("kush_sm100_unpack", *self._fmt, *_pool(cache), H, page_blk.data_ptr(), page_dst.data_ptr(),
+                  n_pages, tail_blk.data_ptr(), tail_info.data_ptr(), n_tail, tail_k.data_ptr(), k_new.data_ptr(),
+                  v_new.data_ptr(), k_new.stride(0), v_new.stride(0), new_dst.data_ptr(), n_new, kp.data_ptr(),
+                  vp.data_ptr(), int(bool(rot)))
 
     # ---------------------------------------------------------------- decode
     def splits(self, num_seqs: int, num_kv_heads: int, max_full_pages: int) -> int:
@@ -165,130 +180,69 @@ class Ops:
         return split_factor(num_seqs, num_kv_heads, max_full_pages, self.sms)
 
     def work_size(self, num_seqs: int, num_kv_heads: int, n_splits: int) -> int:
-        """fp32 elements of the split-KV work buffer: S * Hkv * n_splits * G * (D + 2) (kushkash/_ops.py:195)."""
+        """fp32 elements of the split-KV work buffer: S * Hkv * n_splits * G * (D + 2), the (M, L) pairs first, then
+        the unnormalised outputs (the sizing rule of kushkash/_ops.py:195)."""
         return num_seqs * num_kv_heads * n_splits * self.G * (self.D + 2)
 
+    def _parts(self, S: int, H: int, n_splits: int, work: torch.Tensor | None) -> tuple[int, int]:
+        n_ml = S * H * n_splits * self.G * 2
+        _need(work is not None and work.dtype == torch.float32 and work.is_contiguous()
+              and work.numel() >= self.work_size(S, H, n_splits),
+              f"decode: n_splits={n_splits} needs a contiguous fp32 work buffer of >= "
+              f"{self.work_size(S, H, n_splits)} elements")
+        return work.data_ptr(), work.data_ptr() + 4 * n_ml
+
     def decode(self, q: torch.Tensor, out: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
-               seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor,
-               scale: float, n_splits: int = 1, work: torch.Tensor | None = None, *, rotate: bool = False,
-               order: torch.Tensor | None = None) -> None:
-        """out[s] = attention of q[s] ([Hq, D]) over the seq_lens[s] cached tokens of sequence s
-        (kushkash/_ops.py:191-213).  n_splits > 1 needs `work` (fp32, >= S*Hkv*n_splits*G*(D+2) elements).
-        rotate=True (an extension, for a cache written with rotation): q is rotated inside the kernel and the output
-        rotated back before its store, in place of fwht(q) before and fwht(out) after.  order (an extension): an int32
-        permutation of the S sequences, CTA x decoding sequence order[x] (longest_first()); same outputs."""
+               seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float, n_splits: int = 1,
+               work: torch.Tensor | None = None, *, rotate: bool = False, order: torch.Tensor | None = None) -> None:
+        """out[s] = softmax-scaled attention of q[s] over the seq_lens[s] cached tokens of sequence s.  n_splits > 1
+        splits each sequence's pages over CTAs (split-KV) and merges them with a second launch; it needs `work`
+        (work_size() fp32 elements).  rotate: the cache holds rotated K / V; q is rotated inside the kernel and the
+        output rotated back before its store.  order: a contiguous int32 permutation of the sequences, CTA x then
+        decoding sequence order[x] (longest_first()); the outputs do not depend on it."""
         S, H = q.shape[0], tail_k.shape[1]
-        part_ml = part_o = 0
+        ml = o = 0
         if n_splits > 1:
-            part_ml, part_o = self._parts(S, H, n_splits, work)
-        self._decode(q, out.data_ptr(), cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, part_ml,
-                     part_o, rotate, order)
+            ml, o = self._parts(S, H, n_splits, work)
+        self._decode(q, out.data_ptr(), cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, ml, o,
+                     rotate, order)
         if n_splits > 1:
-            self.k["combine_rotated" if rotate else "combine"]((S, H, 1), 256, out.data_ptr(), part_ml, part_o,
-                                                               n_splits, H)
+            entry = "kush_sm100_combine_rotated" if rotate else "kush_sm100_combine"
+            self._run(entry, self.D, self.cfg.dtype_code, self.G, out.data_ptr(), ml, o, n_splits, H, S)
 
     def decode_partials(self, q: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                         seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float,
                         n_splits: int, work: torch.Tensor) -> tuple[int, int]:
-        """The split-KV decode without its combine (n_splits >= 2): the per-split partials (m, l and unnormalised
-        outputs) in `work`, for a combine that writes elsewhere -- the peer gather of KV-head sharding
-        (kushkash_b200.shard.PeerGather).  Returns the device addresses (part_ml, part_o) inside `work`.  No
-        counterpart in the reference."""
-        if n_splits < 2:
-            raise ValueError("decode_partials needs n_splits >= 2")
+        """The split-KV decode (n_splits >= 2) without its combine: the per-split (M, L) and unnormalised outputs
+        in `work`, for a combine that writes elsewhere (the peer gather of KV-head sharding, shard.PeerGather).
+        Returns their device addresses (part_ml, part_o)."""
+        _need(n_splits >= 2, "decode_partials needs n_splits >= 2")
         S, H = q.shape[0], tail_k.shape[1]
-        part_ml, part_o = self._parts(S, H, n_splits, work)
-        self._decode(q, part_o, cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, part_ml, part_o)
-        return part_ml, part_o
-
-    def _parts(self, S: int, H: int, n_splits: int, work: torch.Tensor | None) -> tuple[int, int]:
-        nml = S * H * n_splits * self.G * 2
-        if work is None or work.dtype != torch.float32 or work.numel() < nml + S * H * n_splits * self.G * self.D:
-            raise ValueError(f"decode: n_splits={n_splits} needs an fp32 work buffer of "
-                             f">= {self.work_size(S, H, n_splits)} elements")
-        return work.data_ptr(), work.data_ptr() + nml * 4
+        ml, o = self._parts(S, H, n_splits, work)
+        self._decode(q, o, cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, ml, o)
+        return ml, o
 
     def _decode(self, q, out_ptr: int, cache, block_table, seq_lens, tail_idx, tail_k, scale: float, n_splits: int,
                 part_ml: int, part_o: int, rotate: bool = False, order: torch.Tensor | None = None) -> None:
         S, H = q.shape[0], tail_k.shape[1]
-        bs, hs = _byte_strides(cache)
-        args = (q.data_ptr(), out_ptr, cache.data_ptr(), bs, hs, tail_k.data_ptr(), tail_idx.data_ptr(),
-                block_table.data_ptr(), seq_lens.data_ptr(), block_table.stride(0), H, float(scale), n_splits, part_ml,
-                part_o)
+        head = (*self._fmt, self.G, q.data_ptr(), out_ptr, *_pool(cache), tail_k.data_ptr(), tail_idx.data_ptr(),
+                block_table.data_ptr(), seq_lens.data_ptr(), block_table.stride(0), H, float(scale), n_splits,
+                part_ml or None, part_o or None, S)
         if order is None:
-            self.k["decode_rotated" if rotate else "decode"]((S, H, n_splits), 32 * self.cfg.warps, *args)
+            self._run("kush_sm100_decode_rotated" if rotate else "kush_sm100_decode", *head)
             return
-        if order.dtype != torch.int32 or order.numel() != S or not order.is_contiguous():
-            raise ValueError("decode: order must be a contiguous int32 permutation of the sequences")
-        self.k["decode_ex"]((S, H, n_splits), 32 * self.cfg.warps, *args, 1 if rotate else 0, order.data_ptr())
+        _need(order.dtype == torch.int32 and order.numel() == S and order.is_contiguous(),
+              "decode: order must be a contiguous int32 permutation of the sequences")
+        self._run("kush_sm100_decode_ex", *head, 1 if rotate else 0, order.data_ptr())
 
     def longest_first(self, seq_lens: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """A launch order for decode(order=): the sequences by full pages, most first (one small kernel; compute it
-        once per step, as the layers share seq_lens).  No counterpart in the reference."""
+        once per step, as the layers share seq_lens)."""
         S = seq_lens.numel()
-        if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
-            raise ValueError("longest_first: seq_lens must be contiguous int32")
-        out = torch.empty(S, dtype=torch.int32, device=seq_lens.device) if out is None else out
-        if out.dtype != torch.int32 or out.numel() != S or not out.is_contiguous():
-            raise ValueError("longest_first: out must be a contiguous int32 tensor of n_seqs entries")
-        self.k["order_longest_first"]((1, 1, 1), 1024, seq_lens.data_ptr(), S, out.data_ptr())
-        return out
-
-
-# ---------------------------------------------------------------- format helpers (pure PyTorch, for tests / callers)
-def as_records(cache: torch.Tensor) -> torch.Tensor:
-    """View any cache tensor ([blocks, H, ...], contiguous records) as uint8 [blocks, H, RB] (kushkash/_ops.py:288-292)."""
-    c = cache.view(torch.uint8) if cache.dtype != torch.uint8 else cache
-    return c.flatten(2) if c.dim() > 3 else c
-
-
-def dequant_records(rec: torch.Tensor, head_dim: int, bits: int, dtype: torch.dtype, page: int = PAGE
-                    ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Records [..., RB] (uint8) -> K, V [..., P, D] in dtype: codes * fp16 scale + fp16 bias
-    (kushkash/_ops.py:217-251)."""
-    D, P = head_dim, page
-    dc = D if bits == 8 else D // 2
-    kq = rec[..., :P * dc].view(torch.int8).unflatten(-1, (P, dc))
-    vq = rec[..., P * dc:2 * P * dc].view(torch.int8).unflatten(-1, (P, dc))
-    meta = rec[..., 2 * P * dc:].contiguous().view(torch.float16)
-    ks, kb = meta[..., :D].unsqueeze(-2), meta[..., D:2 * D].unsqueeze(-2)
-    vs, vb = meta[..., 2 * D:2 * D + P, None], meta[..., 2 * D + P:, None]
-
-    def codes(c):
-        if bits == 4:
-            c = torch.cat([(c << 4) >> 4, c >> 4], -1)
-        return c.to(dtype)
-    return codes(kq) * ks.to(dtype) + kb.to(dtype), codes(vq) * vs.to(dtype) + vb.to(dtype)
-
-
-def cached_kv(records: torch.Tensor, block_ids: torch.Tensor, n: int, tail_k: torch.Tensor, head_dim: int,
-              bits: int, dtype: torch.dtype, page: int = PAGE) -> tuple[torch.Tensor, torch.Tensor]:
-    """The n cached tokens of B sequences as K, V [B, Hk, n, D] (pages dequantized; the partial last page: exact K
-    from tail_k [B, Hk, P, D], V from its record) (kushkash/_ops.py:295-306)."""
-    B, Hk, D, P = block_ids.shape[0], tail_k.shape[1], head_dim, page
-    pages = -(-n // P)
-    k, v = dequant_records(records[block_ids[:, :pages].long()], D, bits, dtype, P)       # [B, p, Hk, P, D]
-    k = k.permute(0, 2, 1, 3, 4).reshape(B, Hk, pages * P, D)
-    v = v.permute(0, 2, 1, 3, 4).reshape(B, Hk, pages * P, D)[:, :, :n]
-    r = n % P
-    k = torch.cat([k[:, :, :n - r], tail_k[:, :, :r].to(dtype)], 2)
-    return k, v
-
-
-def pages_touched(ctx: int, total: int, page: int = PAGE) -> range:
-    """Logical pages written when positions [ctx, total) are added (kushkash/_ops.py:342-344)."""
-    return range(ctx // page, (total - 1) // page + 1) if total > ctx else range(0)
-
-
-def rotation_enabled(bits: int, rotate: bool | None = None) -> bool:
-    """KUSHKASH_ROTATE (auto | 1 | 0; auto = on for 4-bit) unless `rotate` is given (kushkash/_ops.py:350-359)."""
-    if rotate is None:
-        env = os.environ.get("KUSHKASH_ROTATE", "auto")
-        if env not in ("auto", "0", "1"):
-            raise ValueError(f"KUSHKASH_ROTATE must be auto, 0 or 1, got {env}")
-        return bits == 4 if env == "auto" else env == "1"
-    return bool(rotate)
-
-
-def default_scale(head_dim: int) -> float:
-    return 1.0 / math.sqrt(head_dim)
+        _need(seq_lens.dtype == torch.int32 and seq_lens.is_contiguous(), "longest_first: seq_lens must be "
+              "contiguous int32")
+        order = torch.empty(S, dtype=torch.int32, device=seq_lens.device) if out is None else out
+        _need(order.dtype == torch.int32 and order.numel() == S and order.is_contiguous(),
+              "longest_first: out must be a contiguous int32 tensor of n_seqs entries")
+        self._run("kush_sm100_order_longest_first", seq_lens.data_ptr(), S, self.P, order.data_ptr())
+        return order

@@ -81,20 +81,3 @@ def test_split_factor():
     for S, H, n in ((1, 1, 10 ** 6), (3, 5, 999), (64, 8, 8192)):
         ns = split_factor(S, H, n, 148)
         assert 1 <= ns <= 256 and (ns == 1 or n // ns >= 16)
-
-
-def test_dequant_helpers_roundtrip_on_cpu():
-    """cached_kv over oracle-written pages reproduces the quantizer's dequantization (the host-side format view)."""
-    from kushkash_b200 import cached_kv
-    from kushsim import fill, make_state
-    from oracle.kush_oracle import OracleOps
-    for P in (16, 32):
-        B, H, D, n = 2, 2, 64, 3 * P + 3
-        g = torch.Generator().manual_seed(P)
-        K, V = torch.randn(B, H, n, D, generator=g), torch.randn(B, H, n, D, generator=g)
-        bt = torch.randperm(B * 4, generator=g).to(torch.int32).view(B, 4)
-        st = make_state(B, H, D, 8, P, bt, B * 4)
-        fill(OracleOps(D, 8, 1, P), st, K, V, n - 5, torch.float32, "cpu")
-        hk, hv = cached_kv(st.pool, st.block_table, n, st.tail_k, D, 8, torch.float32, P)
-        assert torch.equal(hk[:, :, n - n % P:], K[:, :, n - n % P:])         # exact tail
-        assert (hk - K).abs().max() < 0.05 and (hv - V).abs().max() < 0.05      # int8 pages
