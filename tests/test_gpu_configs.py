@@ -5,7 +5,7 @@ page 32, appends after a bulk prefill) are checked in full against the CPU oracl
 page 16, Llama-3.1-8B heads) and 4 (4 x 131072, int4, page 32, Qwen3-8B heads) are run at full size on the GPU
 and checked on a sample of (sequence, kv head) units: every unit is independent (its own pages, tail and output),
 so the oracle reproduces a unit from that unit's inputs alone -- a size-independent property of the path.  Pages
-must be bit-exact, decode outputs within the bf16 tolerance of the other GPU tests."""
+must be bit-exact, decode outputs within the bf16 bounds of the other GPU tests (max abs 2e-3, rel-norm 1e-2)."""
 import random
 
 import pytest
@@ -13,6 +13,7 @@ import torch
 
 from kushsim import make_state
 from oracle.kush_oracle import OracleOps
+from tolerance import check_decode
 
 pytestmark = pytest.mark.gpu
 
@@ -20,9 +21,7 @@ DT = torch.bfloat16
 
 
 def assert_close(got, want, what):
-    err = (got.float().cpu() - want).abs()
-    bad = err > 2e-3 + 1e-2 * want.abs()
-    assert not bad.any(), f"{what}: {int(bad.sum())} of {bad.numel()} outside tol, max err {err.max().item():.3e}"
+    check_decode(got, want, DT, what)
 
 
 def key_offsets(H, D, gen, outliers, big, spread):
@@ -99,23 +98,27 @@ def check_units(st, ops, K, V, bt, units, G, D, bits, P, seed, dev="cuda", dt=DT
     ops.decode(q.to(device=dev, dtype=dt), out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k,
                D ** -0.5, n_splits, work)
     lens = st.seq_lens.cpu().tolist()
-    pool, tail, out = st.pool.cpu(), st.tail_k.cpu(), out.cpu()
     for s, h in units:
-        n = lens[s]
-        rec, tk, o = oracle_unit(K[s], V[s], q[s, h * G:(h + 1) * G], n, h, G, D, bits, P)
-        pages = -(-n // P)
-        got = pool[bt[s, :pages].long(), h]
-        full = n // P
-        assert torch.equal(got[:full], rec[:full]), (s, h, "full pages")
-        if n % P:                                                       # partial page: V rows and their scales
-            F = 2 * P * (D if bits == 8 else D // 2)
-            dc = D if bits == 8 else D // 2
-            r = n % P
-            assert torch.equal(got[full, P * dc:P * dc + r * dc], rec[full, P * dc:P * dc + r * dc]), (s, h)
-            for a in (F + 4 * D, F + 4 * D + 2 * P):                  # vs, vb of the r rows
-                assert torch.equal(got[full, a:a + 2 * r], rec[full, a:a + 2 * r]), (s, h, "v scales")
-            assert torch.equal(tail[s, h, :r].float(), tk[:r]), (s, h, "tail")
-        assert_close(out[s, h * G:(h + 1) * G], o, f"decode unit {(s, h)}")
+        check_unit(st, bt, out, s, h, lens[s], K[s], V[s], q[s, h * G:(h + 1) * G], G, D, bits, P)
+
+
+def check_unit(st, bt, out, s, h, n, Ks, Vs, qs, G, D, bits, P):
+    """Pages, tail rows and decode output of unit (s, h) on the device against the oracle run on that unit's inputs
+    alone (Ks, Vs: [>= n, H, D] rows of sequence s; qs: its G query rows of kv head h)."""
+    rec, tk, o = oracle_unit(Ks, Vs, qs, n, h, G, D, bits, P)
+    pages = -(-n // P)
+    got = st.pool[bt[s, :pages].long().to(st.pool.device), h].cpu()
+    full = n // P
+    assert torch.equal(got[:full], rec[:full]), (s, h, "full pages")
+    if n % P:                                                       # partial page: V rows and their scales
+        dc = D if bits == 8 else D // 2
+        F = 2 * P * dc
+        r = n % P
+        assert torch.equal(got[full, P * dc:P * dc + r * dc], rec[full, P * dc:P * dc + r * dc]), (s, h)
+        for a in (F + 4 * D, F + 4 * D + 2 * P):                  # vs, vb of the r rows
+            assert torch.equal(got[full, a:a + 2 * r], rec[full, a:a + 2 * r]), (s, h, "v scales")
+        assert torch.equal(st.tail_k[st.tail_idx[s].item(), h, :r].float().cpu(), tk[:r]), (s, h, "tail")
+    assert_close(out[s, h * G:(h + 1) * G].cpu(), o, f"decode unit {(s, h)} n={n}")
 
 
 def test_config1_full():
@@ -151,3 +154,92 @@ def test_config4_full_size_sampled():
                               appends=3)
     assert ops.splits(4, 8, 131072 // 32) > 1
     check_units(st, ops, K, V, bt, [(0, 0), (1, 5), (3, 7)], 4, 128, 4, 32, 4)
+
+
+def test_config5_full_size_sampled():
+    """BASELINE config 5 at its own shape: 2048 decode sequences with lognormal lengths (median 2048, sigma 0.8, cap
+    16384), Llama-3.1-8B heads (32 q / 8 kv, D 128), int4, page 16, key offsets N(0, 2) plus 2 outlier channels at
+    +-15 per kv head.  The caches are filled by ragged bulk writes; then one serving step as bench.py runs it: a bulk
+    prefill-quantize of 32 new 2048-token prompts, a one-token append to every decode sequence and the split-KV
+    decode of all 2048 in longest-first launch order.  64 sampled decode units (the longest and the shortest sequence
+    among them) and 8 prompt units are checked against the oracle run on each unit's inputs alone."""
+    import math
+    S, H, G, D, bits, P, NPR, PL = 2048, 8, 4, 128, 4, 16, 32, 2048
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(S, generator=gen) * 0.8 + math.log(2048)
+    lens = [int(min(16384, max(1, round(math.exp(v))))) for v in x.tolist()]
+    off = key_offsets(H, D, gen, 2, 15.0, 2.0)
+    rng = random.Random(5)
+    picks = set(rng.sample(range(S), 62)) | {max(range(S), key=lens.__getitem__), min(range(S), key=lens.__getitem__)}
+    units = {s: rng.randrange(H) for s in sorted(picks)}
+    pr_units = {p: rng.randrange(H) for p in rng.sample(range(NPR), 8)}
+    pages = [-(-(n + 1) // P) for n in lens]
+    ppr = PL // P
+    n_blocks = sum(pages) + NPR * ppr
+    perm = torch.randperm(n_blocks, generator=gen).to(torch.int32)
+    bt = torch.zeros(S, max(pages), dtype=torch.int32)
+    o = 0
+    for s, p in enumerate(pages):
+        bt[s, :p] = perm[o:o + p]
+        o += p
+    bt_pr = perm[o:].view(NPR, ppr).contiguous()
+    ops = gpu_ops(D, bits, G, P)
+    st = make_state(S, H, D, bits, P, bt, n_blocks, "cuda", DT)
+    pr = make_state(NPR, H, D, bits, P, bt_pr, 1, "cuda", DT)
+    pr.pool = st.pool                                               # prompts and decode sequences share one pool
+    offd = off.cuda()
+    dgen = torch.Generator(device="cuda").manual_seed(55)
+    kept = {}                                                       # sampled units' inputs, on the CPU
+
+    def chunk_write(state, seqs, n_of, tag):
+        s0, s1 = seqs[0], seqs[-1] + 1
+        rows = [n_of(s) for s in range(s0, s1)]
+        T = sum(rows)
+        k = (torch.randn(T, H, D, generator=dgen, device="cuda") + offd).to(DT)
+        v = torch.randn(T, H, D, generator=dgen, device="cuda").to(DT)
+        qsl = torch.tensor([0] + rows, dtype=torch.int64).cumsum(0)
+        npg = [-(-r // P) for r in rows]
+        js = torch.tensor([i for i, m in enumerate(npg) for _ in range(m)], dtype=torch.int32)
+        jp = torch.tensor([j for m in npg for j in range(m)], dtype=torch.int32)
+        state.seq_lens[s0:s1] = torch.tensor(rows, dtype=torch.int32, device="cuda")
+        ops.write(k, v, qsl.to(torch.int32).cuda(), state.seq_lens[s0:s1], state.tail_idx[s0:s1], js.cuda(),
+                  jp.cuda(), state.pool, state.block_table[s0:s1], state.tail_k)
+        for s in range(s0, s1):
+            if (tag, s) in want_rows:
+                a, b = int(qsl[s - s0]), int(qsl[s - s0 + 1])
+                kept[(tag, s)] = (k[a:b].cpu(), v[a:b].cpu())
+
+    want_rows = {("dec", s) for s in units} | {("pr", p) for p in pr_units}
+    chunk, tok = [], 0
+    for s in range(S):                                              # caches: ragged bulk writes of <= 256k tokens
+        if chunk and tok + lens[s] > 262144:
+            chunk_write(st, chunk, lens.__getitem__, "dec")
+            chunk, tok = [], 0
+        chunk.append(s)
+        tok += lens[s]
+    chunk_write(st, chunk, lens.__getitem__, "dec")
+    # the serving step
+    chunk_write(pr, list(range(NPR)), lambda p: PL, "pr")
+    k_new = (torch.randn(S, H, D, generator=dgen, device="cuda") + offd).to(DT)
+    v_new = torch.randn(S, H, D, generator=dgen, device="cuda").to(DT)
+    ops.append(k_new, v_new, st.seq_lens, st.tail_idx, st.pool, st.block_table, st.tail_k, pos_offset=0, advance=True)
+    q = torch.randn(S, H * G, D, generator=dgen, device="cuda").to(DT)
+    ns = ops.splits(S, H, (max(lens) + 1) // P)
+    work = torch.empty(max(1, ops.work_size(S, H, ns)), device="cuda")
+    out = torch.full((S, H * G, D), float("nan"), dtype=DT, device="cuda")
+    order = ops.longest_first(st.seq_lens)
+    ops.decode(q, out, st.pool, st.block_table, st.seq_lens, st.tail_idx, st.tail_k, D ** -0.5, ns, work, order=order)
+    torch.cuda.synchronize()
+    assert st.seq_lens.cpu().tolist() == [n + 1 for n in lens]
+    bt_c = st.block_table.cpu()
+    kn, vn, qc = k_new.cpu(), v_new.cpu(), q.cpu()
+    for s, h in units.items():
+        ks, vs = kept[("dec", s)]
+        Ks, Vs = torch.cat([ks, kn[s:s + 1]]), torch.cat([vs, vn[s:s + 1]])
+        check_unit(st, bt_c, out, s, h, lens[s] + 1, Ks, Vs, qc[s, h * G:(h + 1) * G], G, D, bits, P)
+    btp = pr.block_table.cpu()
+    for p, h in pr_units.items():                                  # prompt pages: bit-exact records
+        ks, vs = kept[("pr", p)]
+        rec, _, _ = oracle_unit(ks, vs, torch.zeros(G, D), PL, h, G, D, bits, P)
+        got = st.pool[btp[p].long().cuda(), h].cpu()
+        assert torch.equal(got, rec), ("prompt", p, h)
