@@ -5,7 +5,7 @@
  * Each entry point replaces one GPU kernel of the reference (kushkash/kush/gpu.mojo), launched by the reference's
  * ctypes loader (kushkash/_cuda.py:92-103, Kernel.__call__) from kushkash/_ops.py.  Arguments keep the reference
  * kernel's order and meaning; what the reference fixes at compile time (head_dim, bits, q-heads-per-kv-head,
- * dtype: kushkash/_build.py:269-306 GpuConfig) and its launch grid become leading / trailing plain arguments, plus
+ * dtype: kushkash/_build.py:112-149 GpuConfig) and its launch grid become leading / trailing plain arguments, plus
  * the page size (16 or 32 tokens; kushkash fixes 32, kushkash/kush/quant.mojo:16).  Every pointer is a device
  * address; strides are in elements unless named *_stride in bytes (block_stride, head_stride).  The kernels run
  * on `stream` (a cudaStream_t; NULL = legacy default stream), allocate nothing and never synchronise the host.
@@ -89,9 +89,9 @@ int kush_sm100_decode(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
  * allocator): the split partials live in a fixed 8 MiB device array inside the library, which every GPU that loads
  * the library holds until exit.  No counterpart in the reference (its decode takes a caller-allocated `work`).
  * Limit: n_seqs * hkv * n_splits * group * (head_dim + 2) <= KUSH_NOALLOC_SCRATCH_FLOATS, else KUSH_ERR_ARG.
- * The first call on each device looks up the array's device address (make it before any stream capture); all
- * calls share the array, so calls that overlap on the GPU race and must be serialised by the caller.  Allocates
- * nothing. */
+ * The first call on each device (and on a context made again after a reset) looks up the array's device address
+ * (make it before any stream capture); all calls share the array, so calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing. */
 int kush_sm100_decode_noalloc(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
                               const void *q, void *out, const void *cache, int64_t block_stride, int64_t head_stride,
                               const void *tail_k, const int32_t *tail_idx, const int32_t *block_table,
@@ -149,7 +149,7 @@ int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page, int32_t d
                          int32_t n_seqs, int32_t flags, const int32_t *order, void *stream);
 
 /* Which decode kernel a configuration takes: 1 = tensor-core kernel (mma), 0 = CUDA-core kernel,
- * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:277-279). */
+ * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:120-122). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);
 
 /* Bounded-wait watchdog of the kernels that wait: bit 0 set if a decode launch gave up waiting for a page copy (its
