@@ -84,6 +84,15 @@ class Geometry:
                 "l2": "inputs larger than L2 (records of 32 layers per step, no flush needed)"}
 
 
+def batch_config(geo: Geometry, world: int, rotate: str = "none") -> dict:
+    """The `config` of a config-3 JSON line; both arms print this same dict (the reference arm describes its
+    bounded host sample in its cpu_baseline)."""
+    return {**geo.describe(), "global_batch": geo.B * world,
+            "parallelism": f"requests partitioned over {world} GPU(s), no collective in the step",
+            "rotation": {"none": "off (as BASELINE)", "fused": "Walsh-Hadamard inside the append and decode kernels",
+                         "unfused": "Walsh-Hadamard by fwht launches around append and decode"}[rotate]}
+
+
 def key_offsets(geo: Geometry, gen: torch.Generator, device) -> torch.Tensor:
     """Per-channel key offsets N(0, 2) plus 2 outlier channels at +-15 per kv head ([Hkv, D])."""
     off = torch.randn(geo.HKV, geo.D, generator=gen) * 2
@@ -222,10 +231,10 @@ class OverlappedIO:
                 t.copy_(self.stage_in[k])
             if i + 1 < steps:
                 in_ready = self._prefetch(main)
-            compute()
+            outs = compute()                                # a step may name this step's output buffers
             if out_done is not None:
                 main.wait_event(out_done)                   # the previous outputs have left the staging
-            for s, o in zip(self.stage_out, self.outputs):
+            for s, o in zip(self.stage_out, self.outputs if outs is None else outs):
                 s.copy_(o)
             self.copy_stream.wait_stream(main)
             with torch.cuda.stream(self.copy_stream):
@@ -373,7 +382,7 @@ def time_cpu_decode(geo: Geometry, smp: dict, budget_s: float, with_append: bool
     """Oracle decode (one task per (sequence, kv head) over all host threads) repeated for ~budget_s seconds."""
     from oracle.kush_oracle import OracleOps, set_threads
     g = geo
-    cores = set_threads(0)
+    cores = set_threads(host_threads())
     ops = OracleOps(g.D, g.bits, g.G, g.P)
     seqs = smp["q"].shape[0]
     out = torch.empty_like(smp["q"])
@@ -393,6 +402,15 @@ def time_cpu_decode(geo: Geometry, smp: dict, budget_s: float, with_append: bool
             "sample": f"layer-steps of {seqs} of the {g.B} sequences x {g.HKV} kv heads at {smp['n']} tokens "
                       f"({iters} decode calls{' + appends' if with_append else ''}, {el:.1f} s)",
             "seconds_per_call": el / iters}
+
+
+def host_threads() -> int:
+    """Host cores this process may run on.  Passed to the oracle explicitly: torchrun sets OMP_NUM_THREADS=1 for its
+    ranks, which would otherwise leave a CPU baseline timed under torchrun on one core."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
 
 
 # ---------------------------------------------------------------- measured peaks
@@ -564,11 +582,7 @@ def main() -> None:
             "warmup": a.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
             "data": "synthetic (seeded bf16 N(0,1) K/V/q with per-channel key offsets, BASELINE config 3 shapes)",
-            "config": {**geo.describe(), "global_batch": geo.B * world,
-                       "parallelism": f"requests partitioned over {world} GPU(s), no collective in the step",
-                       "rotation": {"none": "off (as BASELINE)", "fused": "Walsh-Hadamard inside the append and decode "
-                                    "kernels", "unfused": "Walsh-Hadamard by fwht launches around append and decode"}[
-                           a.rotate]},
+            "config": batch_config(geo, world, a.rotate),
             "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "us_per_layer_step": round(ms_step * 1e3 / geo.L, 2),
             "decode_tokens_per_s": round(geo.B * world / (ms_step / 1e3), 1),
@@ -613,37 +627,54 @@ def run_long(a, world: int, rank: int, local: int) -> None:
         if eng.ns < 2:
             eng.ns = 2
             eng.work = torch.empty(eng.ops.work_size(geo.B, geo.HKV, 2), device=dev)
-        pg = PeerGather(geo.B, full.HQ, geo.D, torch.bfloat16, slots=geo.L)
-        outs = pg.outs
+        # two sets of per-layer slots, alternating per step: a peer's stores of step k+1 land in the other set, and
+        # it cannot start step k+2 before this rank has run step k+1's combines, which its stream orders after the
+        # reads of step k's outputs (PeerGather's slot-reuse rule)
+        pg = PeerGather(geo.B, full.HQ, geo.D, torch.bfloat16, slots=2 * geo.L)
+        out_sets = [pg.outs[:geo.L], pg.outs[geo.L:]]
     else:
         outs = [torch.empty(geo.B, full.HQ, geo.D, dtype=torch.bfloat16, device=dev) for _ in range(geo.L)]
+        out_sets = [outs, outs]
 
-    def step():
+    def step(parity: int = 0):
         for layer in range(geo.L):
             eng.ops.append(eng.k_new[layer], eng.v_new[layer], eng.seq_lens[layer], eng.tail_idx, eng.pool[layer],
                            eng.block_table, eng.tail_k[layer], pos_offset=0, advance=True)
             if pg is not None:
                 decode_gathered(eng.ops, eng.q[layer], eng.pool[layer], eng.block_table, eng.seq_lens[layer],
-                                eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work, pg, layer)
+                                eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work, pg,
+                                parity * geo.L + layer)
                 continue
             eng.ops.decode(eng.q[layer], eng.out[layer], eng.pool[layer], eng.block_table, eng.seq_lens[layer],
                            eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work)
             outs[layer].copy_(gather_heads(eng.out[layer]) if dist is not None else eng.out[layer])
+        return out_sets[parity]
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    steps_done = [0]                            # every rank runs the same sequence of steps, so parities agree
+
+    def eager():
+        steps_done[0] += 1
+        return step((steps_done[0] - 1) % 2)
+
     for _ in range(a.warmup - 1):
-        step()
+        eager()
     graph = None
     if dist is None or pg is not None:          # the whole step as one CUDA graph (no library collective in it)
-        graph = capture(step, dev)
-        run = graph.replay
+        graph = [capture(lambda: step(0), dev), capture(lambda: step(1), dev)]
+
+        def run():
+            p = steps_done[0] % 2
+            steps_done[0] += 1
+            graph[p].replay()
+            return out_sets[p]
     else:                                       # NCCL collectives are never captured: eager steps
-        run = step
-        step()
+        run = eager
+        eager()
     n0 = int(eng.seq_lens[0, 0].item())
     sampler = ClockSampler(local)               # started before the barrier: its spawn cannot skew the ranks
     barrier()
@@ -659,7 +690,7 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     byts = sum(full.packed_bytes(n0 + i + 1) for i in range(a.steps)) * geo.L
     # ---- e2e: q and the new K/V rows of every layer from pinned host memory, every layer's (gathered) outputs back,
     # overlapped with the neighbouring steps (eager NCCL steps: copies around each step on the copy stream as well)
-    io = OverlappedIO({k: getattr(eng, k) for k in ("q", "k_new", "v_new")}, outs, dev)
+    io = OverlappedIO({k: getattr(eng, k) for k in ("q", "k_new", "v_new")}, out_sets[0], dev)
     io.run(1, run)
     n_e2e = int(eng.seq_lens[0, 0].item())
     barrier()
@@ -928,7 +959,7 @@ def time_cpu_ragged(cfg: dict, seqs: list[int], n_prompts: int, budget_s: float)
     """The oracle on the host cores over a sample of a ragged workload (the given sequences at their lengths and
     n_prompts prompts): layer-steps of prompt write + append + decode until budget_s."""
     from oracle.kush_oracle import OracleOps, set_threads
-    cores = set_threads(0)
+    cores = set_threads(host_threads())
     D, H, P, bits, hq = 128, cfg["hkv"], cfg["P"], cfg["bits"], cfg["hq"]
     lens = [cfg["lens"][i] for i in seqs]
     gen = torch.Generator().manual_seed(99)
@@ -1431,8 +1462,10 @@ def run_reference(a, geo: Geometry, world: int, rank: int) -> None:
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4 records, fp32 compute", "impl": "reference",
-            "data": "synthetic (seeded, BASELINE config 3 shapes)", "config": {**geo.describe(),
-            "parallelism": "host cores (OpenMP over (sequence, kv head) tasks)"},
+            "data": "synthetic (seeded, BASELINE config 3 shapes)", "config": batch_config(geo, world),
+            "reference_execution": f"host cores: the reference's CPU algorithm (its C restatement) with OpenMP over "
+                                   f"(sequence, kv head) tasks on {res['cores']} threads, on a bounded sample of the "
+                                   f"workload ({res['sample']})",
             "cpu_baseline": res,
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

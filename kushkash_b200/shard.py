@@ -73,7 +73,15 @@ class PeerGather:
     one CUDA graph.  `slots` buffers (one per layer, say) live in one CUDA-IPC allocation per rank, mapped by every
     other rank at construction (a collective call: all ranks construct together; the handles travel over the
     process group).  Every rank must then make the same sequence of gathers.  Without an initialised process group
-    (or with one rank) the gather is local.  `close()` unmaps and frees (the tensors in `outs` die with it)."""
+    (or with one rank) the gather is local.  `close()` unmaps and frees (the tensors in `outs` die with it).
+
+    Slot reuse.  A wait only proves that every rank has stored the current gather; it says nothing about whether a
+    peer still reads a slot that another gather is about to fill.  What orders a peer's stores: its combine of gather
+    g runs after its wait of gather g - 1, which returns once every rank has run its own combine of gather g - 1.  So
+    with gathers filling slots round robin, a rank's reads of the slot that gather g filled (a copy of the outputs,
+    the next layer's kernels) must be stream-ordered before its own combine of gather g + slots - 1.  One slot per
+    layer and the outputs read after the whole step break this for every layer but the last; give each step its own
+    set of slots (2 x layers, alternating per step) or copy each output out right after its wait."""
 
     def __init__(self, n_seqs: int, num_q_heads: int, head_dim: int, dtype: torch.dtype, slots: int = 1,
                  group=None):
