@@ -1,9 +1,8 @@
 """Generates tests/golden/golden.npz and golden.json from the REFERENCE's own PyTorch pins.
 
-Run in a container where the reference checkout is importable (the directory named by KUSHKASH_REF; nothing at
-test time reads it):
+Run where a checkout of the reference is available (nothing at test time reads it), naming its directory:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <kushkash checkout>        # or KUSHKASH_REF=<checkout> python ...
 
 What it pins, and with which reference function:
   quant   pages written by bulk writes + token appends == the reference's torch quantizer
@@ -33,7 +32,12 @@ sys.path.insert(0, str(HERE))
 from cases import (DECODE_CASES, QUANT_CASES, decode_inputs, fwht_inputs, pack_records, quant_inputs,  # noqa: E402
                    record_bytes, unpack_inputs)
 
-REF = Path(os.environ.get("KUSHKASH_REF", "/root/reference"))
+def reference_dir() -> Path:
+    """The reference checkout: the first command-line argument, else $KUSHKASH_REF; there is no default."""
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KUSHKASH_REF")
+    if not ref:
+        raise SystemExit("usage: make_golden.py <kushkash checkout>  (or set KUSHKASH_REF)")
+    return Path(ref)
 
 
 def sha(t: torch.Tensor) -> str:
@@ -67,8 +71,9 @@ def reference_pool(K, V, n, block_table, n_blocks, D, bits, P, ref_quantize):
 
 
 def main() -> None:
-    sys.path.insert(0, str(REF))
-    sys.path.insert(0, str(REF / "tests"))
+    ref = reference_dir()
+    sys.path.insert(0, str(ref))
+    sys.path.insert(0, str(ref / "tests"))
     import kushkash._ops as kops
     from kushkash._ops import cached_kv, fwht_reference, unpack_reference
     from test_cpu import ref_quantize
