@@ -44,6 +44,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "int4 decode attn: packed-KV HBM GB/s (% of 8 TB/s) and µs/layer-step; tokens/s 1–8 GPU"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+# split-KV decodes merge their splits with a separate combine launch (as the reference's kush_combine);
+# --combine fused merges them inside the decode launch (Ops.decode(fused=True)), measured slower on B200
+FUSED_COMBINE = False
 
 
 # ---------------------------------------------------------------- workload
@@ -123,7 +126,9 @@ class Engine:
         self.offsets = key_offsets(g, gen, device)
         self.scale = 1.0 / math.sqrt(g.D)
         self.ns = self.ops.splits(g.B, g.HKV, g.N // g.P)
-        self.work = torch.empty(max(1, self.ops.work_size(g.B, g.HKV, self.ns)), device=device)
+        self.fused = FUSED_COMBINE
+        # zeros: the fused combine's counters at the end of the work buffer start at 0
+        self.work = torch.zeros(max(1, self.ops.work_size(g.B, g.HKV, self.ns, self.fused)), device=device)
         dgen = torch.Generator(device=device).manual_seed(seed + 1)
         self._fill(dgen)
         # per-step inputs: new token K/V rows and q per layer (bf16), outputs
@@ -175,7 +180,7 @@ class Engine:
         g, ops = self.geo, self.ops
         q = ops.fwht(self.q[layer], out=self.rq) if self.rotate == "unfused" else self.q[layer]
         ops.decode(q, self.out[layer], self.pool[layer], self.block_table, self.seq_lens[layer], self.tail_idx,
-                   self.tail_k[layer], self.scale, self.ns, self.work, rotate=self.rotate == "fused")
+                   self.tail_k[layer], self.scale, self.ns, self.work, rotate=self.rotate == "fused", fused=self.fused)
         if self.rotate == "unfused":
             ops.fwht(self.out[layer], out=self.out[layer])
 
@@ -190,10 +195,12 @@ class Engine:
         g, ops = self.geo, self.ops
         for layer in range(g.L):
             ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.block_table, self.seq_lens[layer],
-                       self.tail_idx, self.tail_k[layer], self.scale, self.ns, self.work, rotate=self.rotate == "fused")
+                       self.tail_idx, self.tail_k[layer], self.scale, self.ns, self.work, rotate=self.rotate == "fused",
+                       fused=self.fused)
 
     def launches_per_step(self) -> int:
-        return self.geo.L * (2 + (1 if self.ns > 1 else 0) + (4 if self.rotate == "unfused" else 0))
+        combine = 1 if self.ns > 1 and not self.fused else 0
+        return self.geo.L * (2 + combine + (4 if self.rotate == "unfused" else 0))
 
 
 class OverlappedIO:
@@ -454,11 +461,16 @@ def main() -> None:
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="config 4 on N > 1 GPUs: outputs gathered by the combine's stores into every rank's buffer "
                          "over NVLink (one CUDA graph per step) or by an NCCL all_gather per layer (eager steps)")
+    ap.add_argument("--combine", choices=["fused", "launch"], default="launch",
+                    help="split-KV decodes: the splits merged by a separate combine launch, as the reference does "
+                         "(launch), or by the last CTA of each unit inside the decode launch (fused)")
     ap.add_argument("--workload", choices=["batch", "long", "mix", "c1", "c2", "unpack"], default="batch",
                     help="batch: config 3 (default, requests partitioned); long: config 4 (kv heads partitioned); "
                          "mix: config 5 (serving mix); c1, c2: configs 1 and 2 (single layer; requests partitioned); "
                          "unpack: prefill with history (packed K/V for a prefill attention)")
     a = ap.parse_args()
+    global FUSED_COMBINE
+    FUSED_COMBINE = a.combine == "fused"
     if a.workload == "long":
         for k, v in (("batch", 4), ("context", 131072), ("page", 32), ("layers", 8)):
             if getattr(a, k) == ap.get_default(k):
@@ -598,7 +610,7 @@ def main() -> None:
             "clocks": clocks,
             "gpu_launches": a.steps * eng.launches_per_step(),
             "decode_kernel": "tensor cores" if eng.ops.cfg.tensor_cores else "cuda cores",
-            "n_splits": eng.ns,
+            "n_splits": eng.ns, "split_combine": "fused" if eng.fused else "launch",
         }
         print(json.dumps(line), flush=True)
     del graph, dgraph
@@ -624,6 +636,7 @@ def run_long(a, world: int, rank: int, local: int) -> None:
     eng = Engine(geo, dev, seed=4321 + rank, extra_tokens=a.warmup + 2 * a.steps + 8)
     pg = None
     if dist is not None and a.gather == "peer":                 # gathered by the combine's peer stores
+        eng.fused = False                                       # the gather is the combine
         if eng.ns < 2:
             eng.ns = 2
             eng.work = torch.empty(eng.ops.work_size(geo.B, geo.HKV, 2), device=dev)
@@ -646,7 +659,7 @@ def run_long(a, world: int, rank: int, local: int) -> None:
                                 parity * geo.L + layer)
                 continue
             eng.ops.decode(eng.q[layer], eng.out[layer], eng.pool[layer], eng.block_table, eng.seq_lens[layer],
-                           eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work)
+                           eng.tail_idx, eng.tail_k[layer], eng.scale, eng.ns, eng.work, fused=eng.fused)
             outs[layer].copy_(gather_heads(eng.out[layer]) if dist is not None else eng.out[layer])
         return out_sets[parity]
 
@@ -717,7 +730,8 @@ def run_long(a, world: int, rank: int, local: int) -> None:
             "config": {**full.describe(), "parallelism": f"kv heads partitioned over {world} GPU(s), outputs "
                        "gathered per layer " + ("by the split-KV combine's stores into every rank's buffer over "
                        "NVLink (CUDA IPC), one wait kernel per layer" if pg is not None else
-                       "by an NCCL all_gather" if dist is not None else "(one GPU: none)"), "n_splits": eng.ns},
+                       "by an NCCL all_gather" if dist is not None else "(one GPU: none)"), "n_splits": eng.ns,
+                       "split_combine": "peer gather" if pg is not None else "fused" if eng.fused else "launch"},
             "pct_of_8TBs": round(100 * value / world / NOMINAL_HBM_GBS, 1),
             "us_per_layer_step": round(ms_step * 1e3 / geo.L, 2),
             "decode_tokens_per_s": round(geo.B / (ms_step / 1e3), 1), "clocks": clocks,
@@ -821,7 +835,8 @@ class RaggedEngine:
         self.offsets = cfg["offsets"](H, D, gen).to(device)
         self.scale = 1.0 / math.sqrt(D)
         self.ns = self.ops.splits(S, H, max(lens) // P) if S else 1
-        self.work = torch.empty(max(1, self.ops.work_size(max(S, 1), H, self.ns)), device=device)
+        self.fused = FUSED_COMBINE
+        self.work = torch.zeros(max(1, self.ops.work_size(max(S, 1), H, self.ns, self.fused)), device=device)
         dgen = torch.Generator(device=device).manual_seed(seed + 1)
         self.fill_in = None
         self._fill(dgen, keep_fill)
@@ -896,7 +911,7 @@ class RaggedEngine:
 
     def decode(self, layer: int) -> None:
         self.ops.decode(self.q[layer], self.out[layer], self.pool[layer], self.bt_dec, self.sl_dec[layer], self.ti_dec,
-                        self.tail_dec[layer], self.scale, self.ns, self.work, order=self.order)
+                        self.tail_dec[layer], self.scale, self.ns, self.work, order=self.order, fused=self.fused)
 
     def step(self) -> None:
         """One step of every layer: the prompts' bulk prefill-quantize (config 5), append + decode of every sequence."""
@@ -938,7 +953,8 @@ class RaggedEngine:
         return self.S * self.HKV * (4 * self.D + self.DC + 4 + 2 * self.D)
 
     def launches_per_step(self) -> int:
-        return (self.L * ((1 if self.PR else 0) + ((2 + (1 if self.ns > 1 else 0)) if self.S else 0))
+        combine = 1 if self.ns > 1 and not self.fused else 0
+        return (self.L * ((1 if self.PR else 0) + ((2 + combine) if self.S else 0))
                 + (1 if self.order is not None else 0))
 
 
@@ -1152,7 +1168,8 @@ def run_ragged(a, world: int, rank: int, local: int, which: str) -> None:
             "e2e": {"value": round(e2e_bytes / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / a.steps, 4), "rank": 0},
             "roofline": roof.get("decode"), "write_roofline": roof.get("write"), "cpu_baseline": cpu,
-            "clocks": clocks, "gpu_launches": a.steps * eng.launches_per_step(), "n_splits": eng.ns}
+            "clocks": clocks, "gpu_launches": a.steps * eng.launches_per_step(), "n_splits": eng.ns,
+            "split_combine": "fused" if eng.fused else "launch"}
         if which == "mix":
             line["decode_tokens_per_s"] = round(S_all / (32 * layer_us / 1e6), 1)
             line["decode_tokens_per_s_is"] = ("2048 decode tokens per 32-layer step, the 32-layer step = 32 x the "

@@ -148,6 +148,23 @@ int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page, int32_t d
                          int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o,
                          int32_t n_seqs, int32_t flags, const int32_t *order, void *stream);
 
+/* kush_sm100_decode_ex followed by its split-KV combine, in ONE launch: the reference's two launches of a split
+ * decode (kush_decode_tc then kush_combine, kushkash/_ops.py:204-211) become one.  For n_splits > 1 every CTA of
+ * (sequence s, kv head h) adds 1 to counters[s * hkv + h] once its partial is in part_ml / part_o, and the last of
+ * them sets the count back to 0 and merges the n_splits partials into out with the arithmetic of
+ * kush_sm100_combine (or kush_sm100_combine_rotated with KUSH_DECODE_ROTATE): out equals that decode + combine bit
+ * for bit.  counters: n_seqs * hkv int32, all 0 before the first call (each call leaves them 0 again).  Two launches
+ * that run at the same time must not share counters.  n_splits = 1 ignores counters.  Configurations the
+ * tensor-core kernel does not build (fp32, large groups) run the CUDA-core decode and kush_sm100_combine as two
+ * launches. */
+int kush_sm100_decode_fused_combine(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group,
+                                    const void *q, void *out, const void *cache, int64_t block_stride,
+                                    int64_t head_stride, const void *tail_k, const int32_t *tail_idx,
+                                    const int32_t *block_table, const int32_t *seq_lens, int64_t max_pages,
+                                    int32_t hkv, float scale, int32_t n_splits, float *part_ml, float *part_o,
+                                    int32_t *counters, int32_t n_seqs, int32_t flags, const int32_t *order,
+                                    void *stream);
+
 /* Which decode kernel a configuration takes: 1 = tensor-core kernel (mma), 0 = CUDA-core kernel,
  * KUSH_ERR_UNSUPPORTED if neither is built.  Mirrors GpuConfig.tensor_cores (kushkash/_build.py:120-122). */
 int kush_sm100_decode_tensor_cores(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, int32_t group);

@@ -179,31 +179,47 @@ class Ops:
         """Split-KV factor for this device (split_factor)."""
         return split_factor(num_seqs, num_kv_heads, max_full_pages, self.sms)
 
-    def work_size(self, num_seqs: int, num_kv_heads: int, n_splits: int) -> int:
+    def work_size(self, num_seqs: int, num_kv_heads: int, n_splits: int, fused: bool = False) -> int:
         """fp32 elements of the split-KV work buffer: S * Hkv * n_splits * G * (D + 2), the (M, L) pairs first, then
-        the unnormalised outputs (the sizing rule of kushkash/_ops.py:195)."""
-        return num_seqs * num_kv_heads * n_splits * self.G * (self.D + 2)
+        the unnormalised outputs (the sizing rule of kushkash/_ops.py:195).  fused: S * Hkv more 32-bit slots at the
+        end, the counters of decode(fused=True) (they must be 0 before the first fused decode: allocate the buffer
+        with torch.zeros; every fused decode leaves them 0)."""
+        return num_seqs * num_kv_heads * (n_splits * self.G * (self.D + 2) + (1 if fused else 0))
 
-    def _parts(self, S: int, H: int, n_splits: int, work: torch.Tensor | None) -> tuple[int, int]:
+    def _parts(self, S: int, H: int, n_splits: int, work: torch.Tensor | None,
+               fused: bool = False) -> tuple[int, int]:
         n_ml = S * H * n_splits * self.G * 2
         _need(work is not None and work.dtype == torch.float32 and work.is_contiguous()
-              and work.numel() >= self.work_size(S, H, n_splits),
+              and work.numel() >= self.work_size(S, H, n_splits, fused),
               f"decode: n_splits={n_splits} needs a contiguous fp32 work buffer of >= "
-              f"{self.work_size(S, H, n_splits)} elements")
+              f"{self.work_size(S, H, n_splits, fused)} elements")
         return work.data_ptr(), work.data_ptr() + 4 * n_ml
 
     def decode(self, q: torch.Tensor, out: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor,
                seq_lens: torch.Tensor, tail_idx: torch.Tensor, tail_k: torch.Tensor, scale: float, n_splits: int = 1,
-               work: torch.Tensor | None = None, *, rotate: bool = False, order: torch.Tensor | None = None) -> None:
+               work: torch.Tensor | None = None, *, rotate: bool = False, order: torch.Tensor | None = None,
+               fused: bool = False) -> None:
         """out[s] = softmax-scaled attention of q[s] over the seq_lens[s] cached tokens of sequence s.  n_splits > 1
         splits each sequence's pages over CTAs (split-KV) and merges them with a second launch; it needs `work`
-        (work_size() fp32 elements).  rotate: the cache holds rotated K / V; q is rotated inside the kernel and the
-        output rotated back before its store.  order: a contiguous int32 permutation of the sequences, CTA x then
-        decoding sequence order[x] (longest_first()); the outputs do not depend on it."""
+        (work_size() fp32 elements).  fused: the merge runs inside the decode launch instead (the last CTA of each
+        (sequence, kv head) merges; the same output bit for bit); `work` then needs work_size(..., fused=True)
+        elements whose last S * Hkv start at 0.  rotate: the cache holds rotated K / V; q is rotated inside the
+        kernel and the output rotated back before its store.  order: a contiguous int32 permutation of the
+        sequences, CTA x then decoding sequence order[x] (longest_first()); the outputs do not depend on it."""
         S, H = q.shape[0], tail_k.shape[1]
         ml = o = 0
         if n_splits > 1:
-            ml, o = self._parts(S, H, n_splits, work)
+            ml, o = self._parts(S, H, n_splits, work, fused)
+        if fused and n_splits > 1:
+            if order is not None:
+                _need(order.dtype == torch.int32 and order.numel() == S and order.is_contiguous(),
+                      "decode: order must be a contiguous int32 permutation of the sequences")
+            counters = ml + 4 * S * H * n_splits * self.G * (self.D + 2)
+            self._run("kush_sm100_decode_fused_combine", *self._fmt, self.G, q.data_ptr(), out.data_ptr(),
+                      *_pool(cache), tail_k.data_ptr(), tail_idx.data_ptr(), block_table.data_ptr(),
+                      seq_lens.data_ptr(), block_table.stride(0), H, float(scale), n_splits, ml, o, counters, S,
+                      1 if rotate else 0, order.data_ptr() if order is not None else None)
+            return
         self._decode(q, out.data_ptr(), cache, block_table, seq_lens, tail_idx, tail_k, scale, n_splits, ml, o,
                      rotate, order)
         if n_splits > 1:

@@ -33,9 +33,15 @@ int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, v
                       int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                       const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
                       int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, const int32_t* order,
-                      cudaStream_t stream);
+                      int32_t* counters, cudaStream_t stream);
 
 }  // namespace kush
+
+extern "C" int kush_sm100_combine(int32_t head_dim, int32_t dtype, int32_t group, void* out, const float* part_ml,
+                                  const float* part_o, int32_t n_splits, int32_t hkv, int32_t n_seqs, void* stream);
+extern "C" int kush_sm100_combine_rotated(int32_t head_dim, int32_t dtype, int32_t group, void* out,
+                                          const float* part_ml, const float* part_o, int32_t n_splits, int32_t hkv,
+                                          int32_t n_seqs, void* stream);
 
 using namespace kush;
 
@@ -62,7 +68,7 @@ static int decode_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
                                  const void* tail_k, const int32_t* tail_idx, const int32_t* block_table,
                                  const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale, int32_t n_splits,
                                  float* part_ml, float* part_o, int32_t n_seqs, int rot, const int32_t* order,
-                                 void* stream) {
+                                 void* stream, int32_t* counters = nullptr) {
     if (n_seqs < 0 || hkv < 1 || group < 1 || n_splits < 1)
         return set_error(KUSH_ERR_ARG, "kush_sm100_decode: n_seqs %d hkv %d group %d n_splits %d", n_seqs, hkv, group,
                          n_splits);
@@ -81,7 +87,7 @@ static int decode_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
     if (decode_mma_supported(head_dim, bits, page, dtype, group))
         return launch_decode_mma(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
                                  tail_idx, block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o,
-                                 n_seqs, rot, order, st);
+                                 n_seqs, rot, order, n_splits > 1 ? counters : nullptr, st);
     g_err[0] = 0;
     int rc = launch_decode_simt_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k,
                                     tail_idx, block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o,
@@ -89,6 +95,9 @@ static int decode_any(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
     if (rc == KUSH_ERR_UNSUPPORTED && g_err[0] == 0)
         return set_error(rc, "kush_sm100_decode: unsupported head_dim %d / bits %d / page %d / dtype %d", head_dim, bits,
                          page, dtype);
+    if (rc == KUSH_OK && counters && n_splits > 1)     // the CUDA-core decode: its combine as a second launch
+        rc = rot ? kush_sm100_combine_rotated(head_dim, dtype, group, out, part_ml, part_o, n_splits, hkv, n_seqs, stream)
+                 : kush_sm100_combine(head_dim, dtype, group, out, part_ml, part_o, n_splits, hkv, n_seqs, stream);
     return rc;
 }
 
@@ -123,4 +132,19 @@ extern "C" int kush_sm100_decode_ex(int32_t head_dim, int32_t bits, int32_t page
     return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
                       block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs,
                       (flags & KUSH_DECODE_ROTATE) ? 1 : 0, order, stream);
+}
+
+extern "C" int kush_sm100_decode_fused_combine(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype,
+                                               int32_t group, const void* q, void* out, const void* cache,
+                                               int64_t block_stride, int64_t head_stride, const void* tail_k,
+                                               const int32_t* tail_idx, const int32_t* block_table,
+                                               const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
+                                               int32_t n_splits, float* part_ml, float* part_o, int32_t* counters,
+                                               int32_t n_seqs, int32_t flags, const int32_t* order, void* stream) {
+    if (flags & ~KUSH_DECODE_ROTATE)
+        return set_error(KUSH_ERR_ARG, "kush_sm100_decode_fused_combine: unknown flags %d", flags);
+    if (n_splits > 1 && !counters) return set_error(KUSH_ERR_ARG, "kush_sm100_decode_fused_combine: null counters");
+    return decode_any(head_dim, bits, page, dtype, group, q, out, cache, block_stride, head_stride, tail_k, tail_idx,
+                      block_table, seq_lens, max_pages, hkv, scale, n_splits, part_ml, part_o, n_seqs,
+                      (flags & KUSH_DECODE_ROTATE) ? 1 : 0, order, stream, counters);
 }

@@ -176,17 +176,20 @@ __device__ __forceinline__ SplitRange split_range(const int32_t* seq_lens, int n
 // The combine of one (sequence, kv head, q head) at output dim d (kushkash/kush/gpu.mojo:469-491): ml points at the
 // first split's (m, l) (natural-log max, sum; split z at ml[2 z G]), po at the first split's unnormalised output
 // for dim d (split z at po[z G D]).  Splits with m = -inf are empty and skipped.  Returns o / L (0 when L = 0).
+// CG: read through L2 only (partials that other CTAs of the same launch have just stored).
+template <bool CG = false>
 __device__ __forceinline__ float merge_splits(const float* __restrict__ ml, const float* __restrict__ po, int n_splits,
                                               int G, int D) {
+    auto ld = [](const float* p) { return CG ? __ldcg(p) : *p; };
     float M = -INFINITY;
-    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ml[2 * int64_t(z) * G]);
+    for (int z = 0; z < n_splits; z++) M = fmaxf(M, ld(ml + 2 * int64_t(z) * G));
     float L = 0.0f, o = 0.0f;
     for (int z = 0; z < n_splits; z++) {
-        const float mz = ml[2 * int64_t(z) * G];
+        const float mz = ld(ml + 2 * int64_t(z) * G);
         if (mz > -INFINITY) {
             const float f = __expf(mz - M);
-            L = fmaf(ml[2 * int64_t(z) * G + 1], f, L);
-            o = fmaf(f, po[int64_t(z) * G * D], o);
+            L = fmaf(ld(ml + 2 * int64_t(z) * G + 1), f, L);
+            o = fmaf(f, ld(po + int64_t(z) * G * D), o);
         }
     }
     return L > 0.0f ? o / L : 0.0f;

@@ -316,6 +316,88 @@ struct MmaCfg {
 // p = exp2(s - m) <= 2^TAU stay far from fp16 overflow in p * vs)
 constexpr float TAU = 4.0f;
 
+// The split-KV combine inside the decode launch (kush_sm100_decode_fused_combine).  Each CTA of (sequence, kv head)
+// sh counts itself on counters[sh] after its partial is stored; the last of the n_splits CTAs sets the count back to
+// 0 (so the counters are ready for the next launch) and merges every split into out.  The arithmetic is merge_splits'
+// (combine_kernel / combine_rot_kernel: the max over the splits, f = e^(m_z - M), L and o accumulated with fmaf in
+// split order, o / L), so the output is bit-identical to the decode followed by kush_sm100_combine(_rotated); the
+// work is laid out for one pass of loads: the (m, l) pairs of the unit (contiguous) and the factors f in shared
+// memory, then each thread's partial outputs with all loads of a head in flight.
+// smem: cap floats of shared memory no longer in use; units whose 3 * n_splits * G + 2 * G (+ G * D with ROT) floats
+// do not fit merge each output straight from global memory (merge_splits, the same arithmetic).
+template <int D, bool ROT, class IN>
+__device__ __noinline__ void combine_if_last(int32_t* counters, int64_t sh, int n_splits, int G,
+                                             const float* part_ml, const float* part_o, IN* out, float* smem, int cap) {
+    __shared__ int last;
+    __threadfence();                                  // this CTA's partial is visible before it is counted
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        last = atomicAdd(&counters[sh], 1) == n_splits - 1;
+        if (last) counters[sh] = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int nz = n_splits * G;
+    const float* ml = part_ml + sh * nz * 2;          // [split][head][m, l] of this unit
+    const float* po = part_o + sh * nz * D;           // [split][head][D]
+    float* sml = smem;                                // the unit's (m, l) pairs
+    float* fz = smem + 2 * nz;                        // f of (split, head)
+    float* sL = fz + nz;                              // L per head
+    float* stage = sL + 2 * G;
+    if (3 * nz + 2 * G + (ROT ? G * D : 0) > cap) {
+        stage = smem;
+        for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+            const int hd = idx / D, d = idx % D;
+            const float r = merge_splits<true>(ml + 2 * hd, po + int64_t(hd) * D + d, n_splits, G, D);
+            if constexpr (ROT) stage[idx] = r;
+            else out[sh * G * D + idx] = from_f32<IN>(r);
+        }
+    } else {
+    for (int i = threadIdx.x; i < 2 * nz; i += blockDim.x) sml[i] = __ldcg(ml + i);
+    __syncthreads();
+    for (int hd = threadIdx.x; hd < G; hd += blockDim.x) {
+        float M = -INFINITY;
+        for (int z = 0; z < n_splits; z++) M = fmaxf(M, sml[2 * (z * G + hd)]);
+        float L = 0.0f;
+        for (int z = 0; z < n_splits; z++) {
+            const float mz = sml[2 * (z * G + hd)];
+            const float f = mz > -INFINITY ? __expf(mz - M) : 0.0f;
+            fz[z * G + hd] = f;
+            if (mz > -INFINITY) L = fmaf(sml[2 * (z * G + hd) + 1], f, L);
+        }
+        sL[hd] = L;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int hd = idx / D, d = idx % D;
+        float o = 0.0f;
+#pragma unroll 4
+        for (int z = 0; z < n_splits; z++) {
+            const float v = __ldcg(po + (int64_t(z) * G + hd) * D + d);
+            if (sml[2 * (z * G + hd)] > -INFINITY) o = fmaf(fz[z * G + hd], v, o);
+        }
+        const float L = sL[hd];
+        const float r = L > 0.0f ? o / L : 0.0f;
+        if constexpr (ROT) stage[idx] = r;
+        else out[sh * G * D + idx] = from_f32<IN>(r);
+    }
+    }
+    if constexpr (ROT) {
+        __syncthreads();
+        constexpr int R = D / WARP;
+        const int lane = threadIdx.x % WARP;
+        for (int hd = threadIdx.x / WARP; hd < G; hd += blockDim.x / WARP) {
+            float x[R];
+#pragma unroll
+            for (int i = 0; i < R; i++) x[i] = stage[hd * D + lane + WARP * i];
+            fwht_warp<D>(x, lane);
+#pragma unroll
+            for (int i = 0; i < R; i++) out[(sh * G + hd) * D + lane + WARP * i] = from_f32<IN>(x[i]);
+        }
+    }
+}
+
 // grid (S, Hkv, n_splits), block 128.  ROT: q rotated in the prologue and the output rotated back before its store;
 // ORD: CTA x works on sequence order[x] (separate instantiations, so the plain kernels keep their code)
 template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD>
@@ -325,7 +407,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     const int32_t* __restrict__ block_table, const int32_t* __restrict__ seq_lens, int64_t max_pages, int H, int G,
     float sm_log2, int n_splits, float* __restrict__ part_ml, float* __restrict__ part_o,
     const __grid_constant__ CUtensorMap tmap, int use_tma, uint32_t swz_m, int32_t rows_per_head, int32_t box_rows,
-    const int32_t* __restrict__ order) {
+    const int32_t* __restrict__ order, int32_t* __restrict__ counters) {
     using F = Fmt<D, BITS, P>;
     using L = Lay<D, BITS>;
     using C = MmaCfg<D, BITS, P, NT>;
@@ -350,6 +432,9 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             part_ml[pb * 2] = -INFINITY;
             part_ml[pb * 2 + 1] = 0.0f;
         }
+        if (counters)
+            combine_if_last<D, ROT>(counters, int64_t(s) * H + h, n_splits, G, part_ml, part_o, out,
+                                    reinterpret_cast<float*>(smem + 1024), (C::SMEM - 1024) / 4);
         return;
     }
     const int64_t p0 = sr.p0, p1 = sr.p1;
@@ -730,6 +815,9 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
             }
         }
     }
+    if (n_splits > 1 && counters)
+        combine_if_last<D, ROT>(counters, int64_t(s) * H + h, n_splits, G, part_ml, part_o, out,
+                                reinterpret_cast<float*>(smem + 1024), (C::SMEM - 1024) / 4);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -780,7 +868,7 @@ template <int D, int BITS, int P, int NT, class IN, bool ROT, bool ORD>
 int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                    const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                    int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
-                   int32_t n_seqs, const int32_t* order, cudaStream_t stream) {
+                   int32_t n_seqs, const int32_t* order, int32_t* counters, cudaStream_t stream) {
     using C = MmaCfg<D, BITS, P, NT>;
     auto kern = decode_mma_kernel<D, BITS, P, NT, IN, ROT, ORD>;
     CUtensorMap map;
@@ -802,7 +890,7 @@ int launch_mma_rot(int G, const void* q, void* out, const void* cache, int64_t b
     launch_pdl(kern, grid, dim3(MMA_NW * WARP), C::SMEM, stream, static_cast<const IN*>(q), static_cast<IN*>(out),
                static_cast<const uint8_t*>(cache), block_stride, head_stride, static_cast<const IN*>(tail_k), tail_idx,
                block_table, seq_lens, max_pages, hkv, G, scale * 1.4426950408889634f, n_splits, part_ml, part_o, map,
-               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order);
+               tma ? 1 : 0, swz_m, rows_per_head, box_rows, order, counters);
     return check_launch("kush_sm100_decode (tensor cores)");
 }
 
@@ -810,18 +898,18 @@ template <int D, int BITS, int P, int NT, class IN>
 int launch_mma(int G, const void* q, void* out, const void* cache, int64_t block_stride, int64_t head_stride,
                const void* tail_k, const int32_t* tail_idx, const int32_t* block_table, const int32_t* seq_lens,
                int64_t max_pages, int32_t hkv, float scale, int32_t n_splits, float* part_ml, float* part_o,
-               int32_t n_seqs, int rot, const int32_t* order, cudaStream_t stream) {
+               int32_t n_seqs, int rot, const int32_t* order, int32_t* counters, cudaStream_t stream) {
     if (rot)                                          // (the rotated decode runs in the natural order)
         return launch_mma_rot<D, BITS, P, NT, IN, true, false>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                tail_idx, block_table, seq_lens, max_pages, hkv, scale,
-                                                               n_splits, part_ml, part_o, n_seqs, nullptr, stream);
+                                                               n_splits, part_ml, part_o, n_seqs, nullptr, counters, stream);
     if (order)
         return launch_mma_rot<D, BITS, P, NT, IN, false, true>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                tail_idx, block_table, seq_lens, max_pages, hkv, scale,
-                                                               n_splits, part_ml, part_o, n_seqs, order, stream);
+                                                               n_splits, part_ml, part_o, n_seqs, order, counters, stream);
     return launch_mma_rot<D, BITS, P, NT, IN, false, false>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                             tail_idx, block_table, seq_lens, max_pages, hkv, scale,
-                                                            n_splits, part_ml, part_o, n_seqs, nullptr, stream);
+                                                            n_splits, part_ml, part_o, n_seqs, nullptr, counters, stream);
 }
 
 int decode_mma_supported(int D, int bits, int P, int dtype, int G) {
@@ -834,7 +922,7 @@ int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, v
                       int64_t block_stride, int64_t head_stride, const void* tail_k, const int32_t* tail_idx,
                       const int32_t* block_table, const int32_t* seq_lens, int64_t max_pages, int32_t hkv, float scale,
                       int32_t n_splits, float* part_ml, float* part_o, int32_t n_seqs, int rot, const int32_t* order,
-                      cudaStream_t stream) {
+                      int32_t* counters, cudaStream_t stream) {
     auto go = [&](auto Dc, auto Bc, auto Pc, auto in) -> int {
         using IN = decltype(in);
         if constexpr (std::is_same_v<IN, float>) {
@@ -842,16 +930,16 @@ int launch_decode_mma(int D, int bits, int P, int dtype, int G, const void* q, v
         } else if constexpr (Dc.value == 256) {
             return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                    tail_idx, block_table, seq_lens, max_pages, hkv,
-                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, order, stream);
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, order, counters, stream);
         } else {
             if (G <= 8)
                 return launch_mma<Dc.value, Bc.value, Pc.value, 1, IN>(G, q, out, cache, block_stride, head_stride,
                                                                        tail_k, tail_idx, block_table, seq_lens,
                                                                        max_pages, hkv, scale, n_splits, part_ml,
-                                                                       part_o, n_seqs, rot, order, stream);
+                                                                       part_o, n_seqs, rot, order, counters, stream);
             return launch_mma<Dc.value, Bc.value, Pc.value, 2, IN>(G, q, out, cache, block_stride, head_stride, tail_k,
                                                                    tail_idx, block_table, seq_lens, max_pages, hkv,
-                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, order, stream);
+                                                                   scale, n_splits, part_ml, part_o, n_seqs, rot, order, counters, stream);
         }
     };
     return dispatch_fmt(D, bits, P, dtype, go);
