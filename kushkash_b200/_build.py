@@ -65,3 +65,21 @@ class GpuConfig:
         return {"append": "kush_sm100_append", "write": "kush_sm100_write",
                 "decode": f"kush_sm100_decode[{'tensor cores' if self.tensor_cores else 'cuda cores'}]",
                 "combine": "kush_sm100_combine", "fwht": "kush_sm100_fwht", "unpack": "kush_sm100_unpack"}
+
+
+def config_class(page: int) -> type:
+    """GpuConfig whose `page` defaults to `page`: what the drop-in installs as kushkash._build.GpuConfig, so that the
+    reference's Ops, which builds GpuConfig(head_dim, bits, group, dtype, arch), gets kernels for that page size."""
+    if page == PAGE:
+        return GpuConfig
+    if page not in (16, 32):
+        raise BuildError(f"page must be 16 or 32, got {page}")
+
+    default = page
+
+    @dataclass(frozen=True)
+    class PagedGpuConfig(GpuConfig):
+        page: int = default
+
+    PagedGpuConfig.__name__ = PagedGpuConfig.__qualname__ = f"GpuConfig{page}"
+    return PagedGpuConfig

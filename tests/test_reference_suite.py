@@ -37,11 +37,25 @@ needs_reference = pytest.mark.skipif(not ((SITE / "kushkash" / "_ops.py").exists
                                      reason=f"no kushkash reference install under {SITE}")
 
 
-def run_reference(files, timeout):
+# At 16-token pages (KUSHKASH_PAGE=16), tests whose fixtures or expected values are written for 32-token pages:
+# they assert kushkash's page-32 constants (page_size 32 declared, 148 * PAGE record bytes), place unpack rows by
+# hand 32 apart (tests/_unpack_case.py), or size a block table at 16 entries for the lengths they write.
+DESELECT_PAGE16 = [
+    "test_cpu.py::test_unpack_cpu_matches_reference", "test_cpu.py::test_unpack_rejects_wrong_dtypes",
+    "test_cpu.py::test_unpack_rejects_bad_indices", "test_cpu.py::test_unpack_rot_equals_rotating_back",
+    "test_ragged.py::test_ragged_mixed_batches", "test_sglang_backend_cpu.py::test_pool_size_and_refused_accessors",
+    "test_sglang_backend_cpu.py::test_server_args_decisions",
+    "test_sglang_backend_cpu.py::test_register_and_resolution_hook_wiring",
+    "test_gpu.py::test_unpack_gpu_matches_reference",
+]
+
+
+def run_reference(files, timeout, page=32, deselect=()):
     env = dict(os.environ)
     env["PYTHONPATH"] = os.pathsep.join([str(SITE), str(ROOT / "tests"), str(ROOT), env.get("PYTHONPATH", "")])
+    env["KUSHKASH_PAGE"] = str(page)
     cmd = [sys.executable, "-m", "pytest", *files, "-p", "refshim", "-q", "-rfE", "-p", "no:cacheprovider"]
-    for d in DESELECT:
+    for d in DESELECT + (DESELECT_PAGE16 if page == 16 else []) + list(deselect):
         if d.split("::")[0] in files:
             cmd += ["--deselect", d]
     r = subprocess.run(cmd, cwd=REF_TESTS, env=env, capture_output=True, text=True, timeout=timeout)
@@ -79,6 +93,17 @@ def test_reference_cpu_suite_over_oracle():
     run_reference(["test_cpu.py", "test_ragged.py", "test_sglang_backend_cpu.py"], timeout=1200)
 
 
+@needs_reference
+def test_reference_cpu_suite_at_page16():
+    """The same reference CPU tests at 16-token pages (BASELINE configs 3 and 5): the drop-in installed with page=16
+    sets kushkash's PAGE constants and GpuConfig, the oracle serves the reference's CPU calls at page 16, and the
+    unmodified SGLang backend (chunked prefill, decode across page boundaries, CUDA-graph metadata, packed prefill)
+    and the reference's page / ragged / decode pins pass; tests/page16_plugin_checks.py adds what the deselected
+    page-32 assertions cover, at page 16 (the plugin declares page_size 16, the pool holds 2624-byte records)."""
+    run_reference(["test_cpu.py", "test_ragged.py", "test_sglang_backend_cpu.py"], timeout=1200, page=16)
+    run_reference([str(ROOT / "tests" / "page16_plugin_checks.py")], timeout=600, page=16)
+
+
 @pytest.mark.gpu
 @needs_reference
 def test_reference_gpu_suite_over_sm100():
@@ -88,3 +113,14 @@ def test_reference_gpu_suite_over_sm100():
     its GPU back end."""
     assert torch.cuda.is_available()
     run_reference(["test_gpu.py"], timeout=1800)
+
+
+@pytest.mark.gpu
+@needs_reference
+def test_reference_gpu_suite_at_page16():
+    """kushkash's tests/test_gpu.py at 16-token pages over libkush_sm100.so (the drop-in installed with page=16): GPU
+    pages byte-identical to the (page-16) CPU path, decode against exact attention, split-K, the HF cache, generate
+    and CUDA-graph generate, FWHT -- everything the reference checks except the unpack case, whose rows are placed by
+    hand for 32-token pages (tests/test_gpu_parity.py checks unpack at page 16)."""
+    assert torch.cuda.is_available()
+    run_reference(["test_gpu.py"], timeout=1800, page=16)
