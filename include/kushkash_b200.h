@@ -60,7 +60,8 @@ int kush_sm100_append(int32_t head_dim, int32_t bits, int32_t page, int32_t dtyp
  * new V rows and, for a page now complete, quantize its K (older rows from the tail, newer from the new rows);
  * mode 1: copy a still-partial page's new K rows into the tail.  The reference launches mode 0 for every job,
  * then mode 1.  mode 2 does both in ONE launch (the tail stash of a sequence runs in the CTA that reads the old
- * tail, after it has read it), with the same result as mode 0 then mode 1. */
+ * tail, after it has read it), with the same result as mode 0 then mode 1.  A job with job_seq[j] < 0 is padding
+ * and is skipped (the lists of kush_sm100_write_jobs, launched with their capacity). */
 int kush_sm100_write(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void *k_new,
                      const void *v_new, int64_t k_stride, int64_t v_stride, const int32_t *query_start_loc,
                      const int32_t *seq_lens, const int32_t *tail_idx, const int32_t *job_seq,
@@ -196,13 +197,41 @@ int kush_sm100_fwht(int32_t head_dim, int32_t dtype, const void *x, void *y, int
  * (kushkash/_ops.py:129-179): full history pages (block page_blk[i] -> rows page_dst[i] + t), partial pages
  * (block tail_blk[i], tail_info[3i..3i+2] = (first row, tokens, tail slot): K from tail_k, V from the record)
  * and new rows (row j of k_new / v_new -> row new_dst[j]) into kp / vp ([rows][hkv][head_dim]).  History is
- * dequantized as fma(code, scale, bias) in fp32, optionally rotated back (rot != 0), rounded once to dtype. */
+ * dequantized as fma(code, scale, bias) in fp32, optionally rotated back (rot != 0), rounded once to dtype.
+ * Entries with page_blk[i] < 0, tail_blk[i] < 0 or new_dst[j] < 0 are padding and are skipped (the plans of
+ * kush_sm100_unpack_plan, launched with their capacities). */
 int kush_sm100_unpack(int32_t head_dim, int32_t bits, int32_t page, int32_t dtype, const void *cache,
                       int64_t block_stride, int64_t head_stride, int32_t hkv, const int32_t *page_blk,
                       const int32_t *page_dst, int32_t n_pages, const int32_t *tail_blk, const int32_t *tail_info,
                       int32_t n_tail, const void *tail_k, const void *k_new, const void *v_new, int64_t k_stride,
                       int64_t v_stride, const int32_t *new_dst, int32_t n_new, void *kp, void *vp, int32_t rot,
                       void *stream);
+
+/* The write jobs of a step, built on the device.  Replaces the per-step host lists of kushkash's serving backends
+ * (kushkash/vllm/backend.py:434-447 _prefill_host, kushkash/sglang/backend.py:255, both over kushkash/_ops.py:343-344
+ * pages_touched, uploaded through the pinned ring of vllm/backend.py:283-312): sequence s, with rows
+ * [query_start_loc[s], query_start_loc[s+1]) ending at position seq_lens[s], gets one job per logical page its rows
+ * touch, ctx / page .. (seq_lens[s] - 1) / page with ctx = seq_lens[s] - its rows, in sequence then page order (the
+ * reference's order).  job_seq / job_page hold max_jobs entries: the jobs, then padding (job_seq = -1) that
+ * kush_sm100_write skips, so the write can be launched with n_jobs = max_jobs without the count coming back to the
+ * host.  *n_jobs (device) = the number of jobs (more than max_jobs means the lists were cut).  max_jobs >= rows /
+ * page + 2 * n_seqs always suffices.  One CTA; no host synchronisation, capture-safe. */
+int kush_sm100_write_jobs(const int32_t *query_start_loc, const int32_t *seq_lens, int32_t n_seqs, int32_t page,
+                          int32_t *job_seq, int32_t *job_page, int32_t max_jobs, int32_t *n_jobs, void *stream);
+
+/* The packed-prefill plan of kush_sm100_unpack for a step, built on the device.  Replaces the host-side plans of
+ * kushkash's serving backends (kushkash/sglang/backend.py:90-110, kushkash/vllm/backend.py:388-413) for a layout that
+ * packs every sequence's history and new rows together: sequence s at rows [kv_start[s], kv_start[s+1]) (kv_start
+ * [n_seqs + 1], the cu_seqlens of a varlen attention), history (ctx = seq_lens[s] - its new rows) first.  Full
+ * history pages -> page_blk / page_dst, the partial history page -> tail_blk / tail_info (first row, tokens,
+ * tail_idx[s]), new row j of the step -> new_dst[j].  Each list is filled to its capacity with padding that
+ * kush_sm100_unpack skips.  counts[4] (device) = full pages, partial pages, new rows, packed rows.  One CTA; no
+ * host synchronisation, capture-safe. */
+int kush_sm100_unpack_plan(const int32_t *query_start_loc, const int32_t *seq_lens, const int32_t *tail_idx,
+                           const int32_t *block_table, int64_t max_pages, int32_t n_seqs, int32_t page,
+                           int32_t *kv_start, int32_t *page_blk, int32_t *page_dst, int32_t max_page_entries,
+                           int32_t *tail_blk, int32_t *tail_info, int32_t max_tail_entries, int32_t *new_dst,
+                           int32_t max_new, int32_t *counts, void *stream);
 
 /* ---- Output gather of KV-head sharding over peer memory (one process per GPU, CUDA IPC over NVLink).
  * Replaces the library all_gather that follows the sharded decode (kushkash_b200/shard.py gather_heads; the

@@ -41,6 +41,8 @@ SIGNATURES = {
     "kush_sm100_decode_ex": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _f32,
                              _i32, _p, _p, _i32, _i32, _p, _p],
     "kush_sm100_order_longest_first": [_p, _i32, _i32, _p, _p],
+    "kush_sm100_write_jobs": [_p, _p, _i32, _i32, _p, _p, _i32, _p, _p],
+    "kush_sm100_unpack_plan": [_p, _p, _p, _p, _i64, _i32, _i32, _p, _p, _p, _i32, _p, _p, _i32, _p, _i32, _p, _p],
     "kush_sm100_decode_fused_combine": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64,
                                         _i32, _f32, _i32, _p, _p, _p, _i32, _i32, _p, _p],
     "kush_sm100_decode_noalloc": [_i32, _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i32,

@@ -132,6 +132,49 @@ class Ops:
                       job_page.data_ptr(), mode, *_pool(cache), tail_k.data_ptr(), *_table(block_table), k.shape[1],
                       n_jobs)
 
+    def write_jobs(self, query_start_loc: torch.Tensor, seq_lens: torch.Tensor, max_jobs: int,
+                   job_seq: torch.Tensor | None = None, job_page: torch.Tensor | None = None,
+                   n_jobs: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """The jobs of write() for a step, built on the device (kush_sm100_write_jobs): one per (sequence, logical
+        page its rows touch), in sequence then page order, then padding to max_jobs that write() skips.  Returns
+        (job_seq, job_page, n_jobs) -- n_jobs a one-element device tensor.  max_jobs >= rows // P + 2 * S always
+        suffices; nothing is read back to the host, so the call can be captured in a CUDA graph."""
+        S = seq_lens.numel()
+        _need(all(t.dtype == torch.int32 and t.is_contiguous() for t in (query_start_loc, seq_lens))
+              and query_start_loc.numel() >= S + 1, "write_jobs: query_start_loc [S + 1] and seq_lens [S] must be "
+              "contiguous int32")
+        dev = seq_lens.device
+        job_seq = torch.empty(max_jobs, dtype=torch.int32, device=dev) if job_seq is None else job_seq
+        job_page = torch.empty(max_jobs, dtype=torch.int32, device=dev) if job_page is None else job_page
+        n_jobs = torch.empty(1, dtype=torch.int32, device=dev) if n_jobs is None else n_jobs
+        _need(job_seq.numel() >= max_jobs and job_page.numel() >= max_jobs and n_jobs.numel() >= 1,
+              "write_jobs: output tensors smaller than max_jobs")
+        self._run("kush_sm100_write_jobs", query_start_loc.data_ptr(), seq_lens.data_ptr(), S, self.P,
+                  job_seq.data_ptr(), job_page.data_ptr(), max_jobs, n_jobs.data_ptr())
+        return job_seq[:max_jobs], job_page[:max_jobs], n_jobs
+
+    def unpack_plan(self, query_start_loc: torch.Tensor, seq_lens: torch.Tensor, tail_idx: torch.Tensor,
+                    block_table: torch.Tensor, max_pages: int, max_tails: int, max_new: int) -> dict:
+        """The plan of unpack() for a step that packs every sequence's history and new rows together (sequence s
+        at rows kv_start[s] .. kv_start[s + 1]), built on the device (kush_sm100_unpack_plan); each list padded to
+        its capacity with entries unpack() skips.  Returns kv_start [S + 1] (the varlen attention's cu_seqlens_k),
+        page_blk, page_dst, tail_blk, tail_info, new_dst and counts [4] (full pages, partial pages, new rows, packed
+        rows), all on the device."""
+        S, dev = seq_lens.numel(), seq_lens.device
+        _need(all(t.dtype == torch.int32 and t.is_contiguous() for t in (query_start_loc, seq_lens, tail_idx))
+              and block_table.dtype == torch.int32 and block_table.stride(1) == 1,
+              "unpack_plan: index tensors must be int32 (query_start_loc, seq_lens, tail_idx contiguous)")
+        i32 = dict(dtype=torch.int32, device=dev)
+        plan = dict(kv_start=torch.empty(S + 1, **i32), page_blk=torch.empty(max_pages, **i32),
+                    page_dst=torch.empty(max_pages, **i32), tail_blk=torch.empty(max_tails, **i32),
+                    tail_info=torch.empty(3 * max_tails, **i32), new_dst=torch.empty(max_new, **i32),
+                    counts=torch.empty(4, **i32))
+        self._run("kush_sm100_unpack_plan", query_start_loc.data_ptr(), seq_lens.data_ptr(), tail_idx.data_ptr(),
+                  *_table(block_table), S, self.P, plan["kv_start"].data_ptr(), plan["page_blk"].data_ptr(),
+                  plan["page_dst"].data_ptr(), max_pages, plan["tail_blk"].data_ptr(), plan["tail_info"].data_ptr(),
+                  max_tails, plan["new_dst"].data_ptr(), max_new, plan["counts"].data_ptr())
+        return plan
+
     # ---------------------------------------------------------------- rotation and unpack
     def fwht(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """The canonical Walsh-Hadamard rotation of every D-row of x (contiguous, this dtype) into out (a new

@@ -41,7 +41,9 @@ __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t* __restrict__
     if (b < n_pages + n_tail) {
         const bool page = b < n_pages;
         const int i = b - n_pages;
-        const uint8_t* rec = cache + int64_t(page ? page_blk[b] : tail_blk[i]) * block_stride + int64_t(h) * head_stride;
+        const int32_t blk = page ? page_blk[b] : tail_blk[i];
+        if (blk < 0) return;                                   // a padding entry (kush_sm100_unpack_plan)
+        const uint8_t* rec = cache + int64_t(blk) * block_stride + int64_t(h) * head_stride;
         const int64_t dst0 = page ? page_dst[b] : tail_info[3 * i];
         const int n = page ? P : tail_info[3 * i + 1];
         float ksv[R], kbv[R];
@@ -77,7 +79,7 @@ __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t* __restrict__
         const int j0 = (b - n_pages - n_tail) * 32;
         for (int t = w; t < 32; t += 4) {
             const int j = j0 + t;
-            if (j < n_new) {
+            if (j < n_new && new_dst[j] >= 0) {
                 const int64_t o = int64_t(new_dst[j]) * rs + int64_t(h) * D;
 #pragma unroll
                 for (int c = 0; c < R; c++) {
@@ -355,7 +357,9 @@ __global__ void __launch_bounds__(256) unpack_vec_kernel(
         const bool page = wi < n_pw;
         const int64_t it = page ? wi : wi - n_pw;
         const int i = int(it / H), h = int(it % H);
-        const uint8_t* rec = cache + int64_t(page ? page_blk[i] : tail_blk[i]) * block_stride + int64_t(h) * head_stride;
+        const int32_t blk = page ? page_blk[i] : tail_blk[i];
+        if (blk < 0) return;                                   // a padding entry (kush_sm100_unpack_plan)
+        const uint8_t* rec = cache + int64_t(blk) * block_stride + int64_t(h) * head_stride;
         const int64_t dst0 = page ? page_dst[i] : tail_info[3 * i];
         const int n = page ? P : tail_info[3 * i + 1];
         const IN* tk = page ? nullptr : tail_k + (int64_t(tail_info[3 * i + 2]) * H + h) * P * D;
@@ -367,6 +371,7 @@ __global__ void __launch_bounds__(256) unpack_vec_kernel(
             unpack_page_vec<D, BITS, P, IN>(rec, tk, n, kout, vout, rs, lane);
     } else if (wi < n_pw + n_tw + n_new) {
         const int64_t j = wi - n_pw - n_tw;
+        if (new_dst[j] < 0) return;                            // a padding entry
         const int64_t o = int64_t(new_dst[j]) * rs;
         if (vec_new) {
             constexpr int E = 16 / int(sizeof(IN));

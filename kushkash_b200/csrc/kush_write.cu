@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(D) write_kernel(const IN* __restrict__ k_new, 
     IN* vs_in = ks_in + P * D;                                      // [P][D] new V rows (row t - ps)
     uint8_t* rs = reinterpret_cast<uint8_t*>(vs_in + P * D);        // [RB] the record, assembled
     const int j = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d % WARP, w = d / WARP;
+    if (job_seq[j] < 0) return;                                     // a padding job (kush_sm100_write_jobs)
     const int64_t s = job_seq[j];
     const int64_t ps = int64_t(job_page[j]) * P;
     const int64_t q0 = qsl[s];
@@ -925,7 +926,7 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
                         int64_t head_stride, IN* tail_k, const int32_t* __restrict__ block_table, int64_t max_pages,
                         int H, int n_jobs) {
     using C = WS<D, BITS, P, IN>;
-    constexpr int FULL = 1 << 30;
+    constexpr int FULL = 1 << 30, SKIP = 1 << 29;                    // item flags beside the kv head in hf
     extern __shared__ __align__(128) uint8_t wss[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(wss + C::OFF_BAR);
     const int lane = threadIdx.x % WARP, w = threadIdx.x / WARP;
@@ -944,7 +945,9 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
     auto load_meta = [&](int batch) {
         WMeta m{0, 0, 0, 0, 0, 0, 0, 0};
         const int64_t it = first + (int64_t(batch) * WARP + lane) * TW;
-        if (it < n_items) {
+        if (it < n_items && job_seq[it / H] < 0) {                  // a padding job: no copy, no encode
+            m.hf = SKIP;
+        } else if (it < n_items) {
             const int64_t j = it / H;
             m.s = job_seq[j];
             m.pg = job_page[j];
@@ -1064,7 +1067,7 @@ __global__ void __launch_bounds__(WS<D, BITS, P, IN>::NW * 32, 3)
                 ws_item<D, BITS, P, IN>(slots + slot * C::STAGE, rec_at(cache, blk, h, block_stride, head_stride),
                                         lane, role);
             }
-        } else if (role == 0) {
+        } else if (role == 0 && !(hf & SKIP)) {
             general(i, l, h, blk);
         }
         __syncwarp();
