@@ -815,7 +815,8 @@ def run_long(a, world: int, rank: int, local: int) -> None:
             "warmup": a.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int4 records, bf16 q/k/v, fp32 softmax",
             "data": "synthetic (seeded bf16 N(0,1) K/V/q with per-channel key offsets N(0, 2), BASELINE config 4 shapes)",
-            "config": {**full.describe(), "parallelism": f"kv heads partitioned over {world} GPU(s), outputs "
+            "config": {**full.describe(), "kv_heads_per_gpu": geo.HKV,
+                       "parallelism": f"kv heads partitioned over {world} GPU(s), outputs "
                        "gathered per layer " + ("by the split-KV combine's stores into every rank's buffer over "
                        "NVLink (CUDA IPC), one wait kernel per layer" if pg is not None else
                        "by an NCCL all_gather" if dist is not None else "(one GPU: none)"), "n_splits": eng.ns,
