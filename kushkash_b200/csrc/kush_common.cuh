@@ -200,10 +200,13 @@ __device__ __forceinline__ float merge_splits(const float* __restrict__ ml, cons
 // stream may be launched as the blocks of the running one exit, and it runs pdl_wait() -- which returns when the
 // previous grid has completed and its memory is visible -- before it touches memory.  Every kernel launched this way
 // starts with pdl_wait(), so the stream order of memory effects is kept; what overlaps is the launch and the block
-// dispatch.  (An explicit early trigger, griddepcontrol.launch_dependents at block start, was measured: config 2's
-// decode step 5% faster, config 4's 2% slower, its waiting blocks resident beside the issue-bound decode; without it
-// config 1 is 4% faster and no configuration slower.)  Without the launch attribute pdl_wait() is a no-op.
+// dispatch.  Only the append triggers its dependent early (pdl_trigger() right after its wait: the decode that follows
+// launches while the short append runs, and its blocks wait in pdl_wait()).  In every kernel at block start the
+// trigger made config 2's step 5% faster but config 4's 2% and config 1's 4% slower, the waiting blocks resident
+// beside the issue-bound decode; in the append alone: config 2 -5%, config 5 -0.4 to -1.2%, config 4 -0.5%, configs 1
+// and 3 unchanged.  Without the launch attribute pdl_wait() and pdl_trigger() are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 template <class... KArgs, class... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(D) append_kernel(const IN* __restrict__ k_new,
                                                    const int32_t* __restrict__ block_table, int64_t max_pages, int H,
                                                    int rot) {
     pdl_wait();                                       // previous kernel on the stream done
+    pdl_trigger();                                    // the decode after it may launch (it waits for this grid)
     const int s = blockIdx.x, d = threadIdx.x, lane = d % WARP, w = d / WARP;
     constexpr int NW = D / WARP, R = D / WARP;
     const int64_t pos = int64_t(seq_lens[s]) + pos_offset;
