@@ -200,11 +200,13 @@ __device__ __forceinline__ float merge_splits(const float* __restrict__ ml, cons
 // stream may be launched as the blocks of the running one exit, and it runs pdl_wait() -- which returns when the
 // previous grid has completed and its memory is visible -- before it touches memory.  Every kernel launched this way
 // starts with pdl_wait(), so the stream order of memory effects is kept; what overlaps is the launch and the block
-// dispatch.  Only the append triggers its dependent early (pdl_trigger() right after its wait: the decode that follows
-// launches while the short append runs, and its blocks wait in pdl_wait()).  In every kernel at block start the
-// trigger made config 2's step 5% faster but config 4's 2% and config 1's 4% slower, the waiting blocks resident
-// beside the issue-bound decode; in the append alone: config 2 -5%, config 5 -0.4 to -1.2%, config 4 -0.5%, configs 1
-// and 3 unchanged.  Without the launch attribute pdl_wait() and pdl_trigger() are no-ops.
+// dispatch.  Two kernels trigger their dependent early (pdl_trigger() right after their wait, so the next launch's
+// blocks are placed while they run and wait in pdl_wait()): the append (the decode after it launches while the short
+// append runs: config 2 -5%, config 5 -0.4 to -1.2%, config 4 -0.5%, configs 1 and 3 unchanged) and the decode
+// without splits (the next layer's kernels launch behind its last wave: config 5 -2.3%, config 3 -0.2%).  In every
+// kernel at block start, the split decodes included, the trigger made config 4's step 2% and config 1's 4% slower,
+// the waiting blocks resident beside the issue-bound decode; in the split combine it measured neutral.  Without the
+// launch attribute pdl_wait() and pdl_trigger() are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 

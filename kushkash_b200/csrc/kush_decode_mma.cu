@@ -413,6 +413,7 @@ __global__ void __launch_bounds__(MMA_NW * WARP, (MmaCfg<D, BITS, P, NT>::MINB))
     using C = MmaCfg<D, BITS, P, NT>;
     constexpr int NW = MMA_NW, NS = C::NS, KT = L::KT, MT = L::MT, MTT = P / 16;
     pdl_wait();                                                         // previous kernel on the stream done
+    if (n_splits == 1) pdl_trigger();         // no combine follows: the next launch may start behind the last wave
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // [NW][NS]
     const uint32_t smem0 = smem_u32(smem);
